@@ -1,0 +1,348 @@
+// Memory-bound passes around the fused GEMMs. One warp per row everywhere; these
+// kernels stream HBM and are sized for it (8 warps per block, grid = rows / 8).
+//
+//   ln_stats_kernel      per-256-column (mean, M2) of the first block's input rows
+//                        (+ bf16 / fp32 copies); stats format = wdit_gemm_residual's.
+//   fold_weight_kernel   per-step adaLN fold into the next Linear: W' = W * mult[k],
+//                        csum[n] = sum_k W'[n,k], vec[n] = sum_k shift[k] W[n,k] + b[n].
+//   layernorm_mod_kernel reference op coda_wan/wan_coda_kernels.py:35-81.
+//   rmsnorm_kernel       reference op coda_wan/wan_coda_kernels.py:371-411.
+//   qk_rms_rope_kernel   reference op coda_wan/wan_coda_kernels.py:233-352.
+//   rope_table_kernel    reference op coda_wan/wan_coda_kernels.py:414-430.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "wdit_internal.h"
+
+namespace wdit {
+namespace {
+
+constexpr int kRowsPerBlock = 8;
+constexpr int kSeg = 256;  // statistics tile width (= the GEMM's BN)
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void load8(const void* base, bool is_bf16, size_t idx, float (&v)[8]) {
+  if (is_bf16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + idx);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+    const float4 a = p[0], b = p[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+__device__ __forceinline__ void store8_bf16(void* base, size_t idx, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + idx) = u;
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) ln_stats_kernel(const void* __restrict__ x, int is_bf16, int ldx, int M, int D,
+                                                       float* __restrict__ stats, void* __restrict__ xb,
+                                                       float* __restrict__ xf) {
+  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const int nseg = (D + kSeg - 1) / kSeg;
+  for (int sgi = 0; sgi < nseg; ++sgi) {
+    const int c0 = sgi * kSeg + lane * 8;
+    const int width = min(kSeg, D - sgi * kSeg);
+    const bool ok = c0 < D;
+    float v[8];
+    if (ok) {
+      load8(x, is_bf16 != 0, static_cast<size_t>(row) * ldx + c0, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[i];
+    const float mean = warp_sum(s) / static_cast<float>(width);
+    float m2 = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[i] - mean;
+        m2 = fmaf(d, d, m2);
+      }
+    }
+    m2 = warp_sum(m2);
+    if (lane == 0) {
+      *reinterpret_cast<float2*>(stats + (static_cast<size_t>(row) * nseg + sgi) * 2) = make_float2(mean, m2);
+    }
+    if (ok && xb != nullptr) store8_bf16(xb, static_cast<size_t>(row) * D + c0, v);
+    if (ok && xf != nullptr) {
+      float4* p = reinterpret_cast<float4*>(xf + static_cast<size_t>(row) * D + c0);
+      p[0] = make_float4(v[0], v[1], v[2], v[3]);
+      p[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    fold_weight_kernel(const __nv_bfloat16* __restrict__ W, int ldw, int N, int K, float mult_c,
+                       const float* __restrict__ ma, const float* __restrict__ mb, const float* __restrict__ sa,
+                       const float* __restrict__ sb, const float* __restrict__ bias, __nv_bfloat16* __restrict__ Wout,
+                       int ldo, float* __restrict__ csum, float* __restrict__ vec) {
+  const int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (n >= N) return;
+  float cs = 0.f, vs = 0.f;
+  for (int k0 = lane * 8; k0 < K; k0 += 256) {
+    float w[8];
+    load8(W, true, static_cast<size_t>(n) * ldw + k0, w);
+    float m[8], sh[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = ma != nullptr ? __ldg(ma + k0 + i) : 0.f;
+      const float b = mb != nullptr ? __ldg(mb + k0 + i) : 0.f;
+      m[i] = mult_c + (a + b);
+      const float s0 = sa != nullptr ? __ldg(sa + k0 + i) : 0.f;
+      const float s1 = sb != nullptr ? __ldg(sb + k0 + i) : 0.f;
+      sh[i] = s0 + s1;
+    }
+    float wf[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      wf[i] = __bfloat162float(__float2bfloat16_rn(w[i] * m[i]));
+      cs += wf[i];
+      vs = fmaf(sh[i], w[i], vs);
+    }
+    store8_bf16(Wout, static_cast<size_t>(n) * ldo + k0, wf);
+  }
+  cs = warp_sum(cs);
+  vs = warp_sum(vs);
+  if (lane == 0) {
+    csum[n] = cs;
+    vec[n] = vs + (bias != nullptr ? bias[n] : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row-wise two-pass LayerNorm + modulation, the row re-read from L1/L2 between passes.
+__global__ void __launch_bounds__(256)
+    layernorm_mod_kernel(const void* __restrict__ x, int is_bf16, int ldx, int M, int D,
+                         const float* __restrict__ scale, const float* __restrict__ shift, float eps,
+                         __nv_bfloat16* __restrict__ out, int ldo) {
+  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const size_t base = static_cast<size_t>(row) * ldx;
+  float s = 0.f;
+  for (int c = lane * 8; c < D; c += 256) {
+    float v[8];
+    load8(x, is_bf16 != 0, base + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[i];
+  }
+  const float mean = warp_sum(s) / static_cast<float>(D);
+  float q = 0.f;
+  for (int c = lane * 8; c < D; c += 256) {
+    float v[8];
+    load8(x, is_bf16 != 0, base + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = v[i] - mean;
+      q = fmaf(d, d, q);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(D) + eps);
+  for (int c = lane * 8; c < D; c += 256) {
+    float v[8];
+    load8(x, is_bf16 != 0, base + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (v[i] - mean) * rstd * (1.0f + scale[c + i]) + shift[c + i];
+    store8_bf16(out, static_cast<size_t>(row) * ldo + c, v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M, int D,
+                                                      const float* __restrict__ w, float eps,
+                                                      __nv_bfloat16* __restrict__ out, int ldo) {
+  const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const size_t base = static_cast<size_t>(row) * ldx;
+  float q = 0.f;
+  for (int c = lane * 8; c < D; c += 256) {
+    float v[8];
+    load8(x, true, base + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q = fmaf(v[i], v[i], q);
+  }
+  const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(D) + eps);
+  for (int c = lane * 8; c < D; c += 256) {
+    float v[8];
+    load8(x, true, base + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y = __bfloat162float(__float2bfloat16_rn(v[i] * rstd));
+      v[i] = y * w[c + i];
+    }
+    store8_bf16(out, static_cast<size_t>(row) * ldo + c, v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One warp per (row, half): half 0 = q, half 1 = k, each D wide, normalized in place.
+__global__ void __launch_bounds__(256)
+    qk_rms_rope_kernel(__nv_bfloat16* __restrict__ qk, int ldqk, const float* __restrict__ partial, int M, int D,
+                       const float* __restrict__ wq, const float* __restrict__ wk, const float* __restrict__ cs,
+                       const float* __restrict__ sn, float eps) {
+  const int item = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int row = item >> 1;
+  const int half = item & 1;
+  if (row >= M) return;
+  const int parts = D / 128;
+  float ms = 0.f;
+  for (int j = lane; j < parts; j += 32) ms += partial[static_cast<size_t>(row) * 2 * parts + half * parts + j];
+  ms = warp_sum(ms) / static_cast<float>(parts);
+  const float rstd = rsqrtf(ms + eps);
+  const float* w = half == 0 ? wq : wk;
+  __nv_bfloat16* base = qk + static_cast<size_t>(row) * ldqk + half * D;
+  for (int c = lane * 8; c < D; c += 256) {
+    float v[8];
+    load8(base, true, c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y = __bfloat162float(__float2bfloat16_rn(v[i] * rstd));
+      v[i] = __bfloat162float(__float2bfloat16_rn(y * w[c + i]));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pair = ((c + 2 * i) & 127) >> 1;
+      const float cc = cs[static_cast<size_t>(row) * 64 + pair];
+      const float ss = sn[static_cast<size_t>(row) * 64 + pair];
+      const float e = v[2 * i], o = v[2 * i + 1];
+      v[2 * i] = e * cc - o * ss;
+      v[2 * i + 1] = e * ss + o * cc;
+    }
+    store8_bf16(base, c, v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+__global__ void rope_table_kernel(const double* __restrict__ freqs_ri, int max_pos, int f, int h, int w,
+                                  float* __restrict__ cos_out, float* __restrict__ sin_out) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(f) * h * w * 64;
+  if (idx >= total) return;
+  const int pair = static_cast<int>(idx & 63);
+  const long long tok = idx >> 6;
+  const int wi = static_cast<int>(tok % w);
+  const int hi = static_cast<int>((tok / w) % h);
+  const int fi = static_cast<int>(tok / (static_cast<long long>(w) * h));
+  // Column split [22, 21, 21]: frame, height, width (head_dim 128 -> 44/42/42 dims).
+  const int pos = pair < 22 ? fi : (pair < 43 ? hi : wi);
+  const double re = freqs_ri[(static_cast<size_t>(pos) * 64 + pair) * 2];
+  const double im = freqs_ri[(static_cast<size_t>(pos) * 64 + pair) * 2 + 1];
+  cos_out[idx] = static_cast<float>(re);
+  sin_out[idx] = static_cast<float>(im);
+}
+
+inline int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? WDIT_OK : WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+}
+
+inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+inline unsigned row_blocks(int rows) { return static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock); }
+
+}  // namespace
+}  // namespace wdit
+
+using namespace wdit;
+
+extern "C" {
+
+int wdit_ln_stats(const void* x, int x_is_bf16, int ldx, int M, int D, float* stats_out, void* x_bf16_out,
+                  float* x_f32_out, void* stream) {
+  if (x == nullptr || stats_out == nullptr) return WDIT_ERR_ARG;
+  if (M <= 0 || D <= 0 || D % 8 != 0 || ldx < D) return WDIT_ERR_SHAPE;
+  if (!a16(x) || ldx % 8 != 0 || (reinterpret_cast<uintptr_t>(stats_out) & 7) != 0) return WDIT_ERR_ALIGN;
+  if ((x_bf16_out && !a16(x_bf16_out)) || (x_f32_out && !a16(x_f32_out))) return WDIT_ERR_ALIGN;
+  if (M == 0) return WDIT_OK;
+  ln_stats_kernel<<<row_blocks(M), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, x_is_bf16, ldx, M, D, stats_out,
+                                                                                 x_bf16_out, x_f32_out);
+  return launch_status();
+}
+
+int wdit_fold_weight(const void* W, int ldw, int N, int K, float mult_c, const float* mult_a, const float* mult_b,
+                     const float* shift_a, const float* shift_b, const float* bias, void* W_out, int ldw_out,
+                     float* csum_out, float* vec_out, void* stream) {
+  if (W == nullptr || W_out == nullptr || csum_out == nullptr || vec_out == nullptr) return WDIT_ERR_ARG;
+  if (N <= 0 || K <= 0 || K % 8 != 0 || ldw < K || ldw_out < K) return WDIT_ERR_SHAPE;
+  if (!a16(W) || !a16(W_out) || ldw % 8 != 0 || ldw_out % 8 != 0) return WDIT_ERR_ALIGN;
+  fold_weight_kernel<<<row_blocks(N), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(W), ldw, N, K, mult_c, mult_a, mult_b, shift_a, shift_b, bias,
+      reinterpret_cast<__nv_bfloat16*>(W_out), ldw_out, csum_out, vec_out);
+  return launch_status();
+}
+
+int wdit_layernorm_modulation(const void* x, int x_is_bf16, int ldx, int M, int D, const float* scale,
+                              const float* shift, float eps, void* out, int ldo, void* stream) {
+  if (x == nullptr || scale == nullptr || shift == nullptr || out == nullptr) return WDIT_ERR_ARG;
+  if (M <= 0 || D <= 0 || D % 8 != 0 || ldx < D || ldo < D) return WDIT_ERR_SHAPE;
+  if (!a16(x) || !a16(out) || ldx % 8 != 0 || ldo % 8 != 0) return WDIT_ERR_ALIGN;
+  layernorm_mod_kernel<<<row_blocks(M), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, x_is_bf16, ldx, M, D, scale, shift, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  return launch_status();
+}
+
+int wdit_rmsnorm(const void* x, int ldx, int M, int D, const float* w, float eps, void* out, int ldo, void* stream) {
+  if (x == nullptr || w == nullptr || out == nullptr) return WDIT_ERR_ARG;
+  if (M <= 0 || D <= 0 || D % 8 != 0 || ldx < D || ldo < D) return WDIT_ERR_SHAPE;
+  if (!a16(x) || !a16(out) || ldx % 8 != 0 || ldo % 8 != 0) return WDIT_ERR_ALIGN;
+  rmsnorm_kernel<<<row_blocks(M), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, D, w, eps, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  return launch_status();
+}
+
+int wdit_qk_rms_rope_from_partials(void* qk, int ldqk, const float* partial, int M, int D, const float* wq,
+                                   const float* wk, const float* cos_tab, const float* sin_tab, float eps,
+                                   void* stream) {
+  if (qk == nullptr || partial == nullptr || wq == nullptr || wk == nullptr || cos_tab == nullptr ||
+      sin_tab == nullptr)
+    return WDIT_ERR_ARG;
+  if (M <= 0 || D <= 0 || D % 128 != 0 || ldqk < 2 * D) return WDIT_ERR_SHAPE;
+  if (!a16(qk) || ldqk % 8 != 0) return WDIT_ERR_ALIGN;
+  qk_rms_rope_kernel<<<row_blocks(2 * M), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<__nv_bfloat16*>(qk), ldqk, partial, M, D, wq, wk, cos_tab, sin_tab, eps);
+  return launch_status();
+}
+
+int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, float* cos_out, float* sin_out,
+                    void* stream) {
+  if (freqs_ri == nullptr || cos_out == nullptr || sin_out == nullptr) return WDIT_ERR_ARG;
+  if (f <= 0 || h <= 0 || w <= 0 || f > max_pos || h > max_pos || w > max_pos) return WDIT_ERR_SHAPE;
+  const long long total = static_cast<long long>(f) * h * w * 64;
+  const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+  rope_table_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(freqs_ri, max_pos, f, h, w, cos_out,
+                                                                            sin_out);
+  return launch_status();
+}
+
+}  // extern "C"

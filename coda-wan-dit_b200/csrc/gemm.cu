@@ -1,0 +1,947 @@
+// Persistent warp-specialized tcgen05 GEMM with the Wan block's fused epilogues.
+//
+//   D[M, N] = A[M, K] . B[N, K]^T      A, B bf16 K-major (B = nn.Linear.weight layout),
+//                                       fp32 accumulation in TMEM.
+//
+// CTA = 6 warps, one CTA per SM, grid = min(#SMs, #tiles), static tile order
+// tile -> (m_blk = tile / n_blocks, n_blk = tile % n_blocks):
+//   warp 0     TMA producer: A (128x64) and B (256x64) tiles, 128-byte swizzle,
+//              STAGES-deep shared-memory ring (full/empty mbarriers).
+//   warp 1     TMEM allocator (512 columns = two 128x256 fp32 accumulators) and
+//              single-thread tcgen05.mma issuer (M=128, N=256, K=16 per instruction).
+//   warps 2-5  epilogue: tcgen05.ld (thread = one accumulator row), fused math,
+//              swizzled shared-memory staging, TMA stores.
+// The accumulator is double buffered, so the epilogue of tile i overlaps the
+// mainloop of tile i+1.
+//
+// Epilogue families (one template instance each):
+//   kEpiAct       out_bf16 = act( LN(acc) + vec )          FFN1 (tanh-GELU), plain bias GEMMs
+//   kEpiResidual  out_f32  = C + (acc + bias) * gate        self-O / FFN2 (gate), cross-O (no gate)
+//                 and optionally a bf16 copy of out plus per-row (mean, M2) partials
+//                 of out over each 256-column tile (the next LayerNorm's statistics).
+//   kEpiNorm      out_bf16 = RoPE( RMSNorm_fullwidth( LN(acc) + vec ) )   QKV, cross-Q, cross-KV
+//                 The full-width RMSNorm needs the sum of squares over D = 1536 (or 5120)
+//                 columns, i.e. over D/256 tiles owned by different CTAs; each tile
+//                 publishes its per-row partial to a global scratch slot and a per
+//                 (row block, group) arrival counter, waits (bounded) for the group, then
+//                 normalizes straight out of TMEM. This kernel is launched cooperatively so
+//                 all CTAs are co-resident (the wait cannot deadlock).
+//
+// LN(acc) is the adaLN LayerNorm absorbed into the GEMM (the modulation scale is folded
+// into the weight each step):  LN(acc) = rstd * (acc - mu * csum[n]),
+// with (mu, rstd) merged from the (mean, M2) partials emitted by the previous residual
+// epilogue (Chan's parallel variance merge), and the shift term added through `vec`.
+//
+// Reference counterparts (Owen718/CODA-Wan-DiT):
+//   kEpiAct       coda_wan/wan_coda_kernels.py:84-152   (EVTGELUBias, linear_bias_gelu_fixed)
+//   kEpiResidual  coda_wan/wan_gate_residual_coda.py:75-135, 138-161, 192-242
+//   kEpiNorm      coda_wan/wan_coda_kernels.py:155-352 (Q+K GEMM with mean-square partials +
+//                 _qk_rms_rope_kernel) and :371-411 (_rmsnorm_kernel)
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "ptx.cuh"
+#include "wdit_internal.h"
+
+namespace wdit {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr uint32_t kTileABytes = BM * BK * 2;  // 16 KB
+constexpr uint32_t kTileBBytes = BN * BK * 2;  // 32 KB
+constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+constexpr int kTmemCols = 2 * BN;  // two accumulator buffers
+
+enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiNorm = 2 };
+
+template <int KIND>
+struct Cfg;
+template <>
+struct Cfg<kEpiAct> {
+  static constexpr int kStages = 4;
+  static constexpr uint32_t kEpiBytes = 2 * 16384;  // 2 x (128 rows x 64 bf16), 128B swizzle
+  static constexpr int kNumCBuf = 0;
+};
+template <>
+struct Cfg<kEpiNorm> {
+  static constexpr int kStages = 4;
+  static constexpr uint32_t kEpiBytes = 2 * 16384;
+  static constexpr int kNumCBuf = 0;
+};
+template <>
+struct Cfg<kEpiResidual> {
+  static constexpr int kStages = 3;
+  static constexpr int kNumCBuf = 4;  // 128 rows x 32 fp32 (16 KB) residual/out ring
+  static constexpr uint32_t kEpiBytes = kNumCBuf * 16384 + 2 * 8192;  // + 2 x (128 x 32 bf16)
+};
+
+template <int KIND>
+constexpr uint32_t smem_bytes() {
+  return 1024 /*alignment slack*/ + Cfg<KIND>::kStages * kStageBytes + Cfg<KIND>::kEpiBytes +
+         256 /*barriers + tmem slot*/;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))); constants as in
+  // coda_wan/wan_coda_kernels.py:100-101.
+  const float z = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanh_approx(z));
+}
+
+// Merge per-tile (mean, M2) partials of one row into (mu, rstd).
+__device__ __forceinline__ void ln_row_stats(const LnFold& ln, int row, float& mu, float& rstd) {
+  const float* st = ln.stats + static_cast<size_t>(row) * ln.stats_tiles * 2;
+  float n = 0.f, mean = 0.f, m2 = 0.f;
+  for (int t = 0; t < ln.stats_tiles; ++t) {
+    const float2 pm = *reinterpret_cast<const float2*>(st + 2 * t);
+    const int rem = ln.row_len - t * ln.stats_width;
+    const float nt = static_cast<float>(rem < ln.stats_width ? rem : ln.stats_width);
+    const float tot = n + nt;
+    const float delta = pm.x - mean;
+    mean += delta * (nt / tot);
+    m2 += pm.y + delta * delta * (n * nt / tot);
+    n = tot;
+  }
+  mu = mean;
+  rstd = rsqrtf(m2 / static_cast<float>(ln.row_len) + ln.eps);
+}
+
+// Write 64 bf16 values (32 packed words) of row r into a 128-byte-swizzled staging tile.
+__device__ __forceinline__ void stage_row_sw128(uint32_t tile_addr, int r, const uint32_t (&w)[32]) {
+  const uint32_t row_addr = tile_addr + r * 128;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t a = row_addr + ((q ^ (r & 7)) << 4);
+    st_shared_v4(a, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  }
+}
+
+// Load 64 consecutive fp32 values of a per-column vector (broadcast across the warp).
+__device__ __forceinline__ void load_vec64(const float* __restrict__ v, int n0, float (&out)[64]) {
+  const float4* p = reinterpret_cast<const float4*>(v + n0);
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const float4 t = __ldg(p + q);
+    out[4 * q] = t.x;
+    out[4 * q + 1] = t.y;
+    out[4 * q + 2] = t.z;
+    out[4 * q + 3] = t.w;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmC,
+                const __grid_constant__ CUtensorMap tmX, const GemmShape s, const EpiParams p) {
+  constexpr int STAGES = Cfg<KIND>::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_base = smem;
+  uint8_t* epi_base = smem + STAGES * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_base + Cfg<KIND>::kEpiBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* tfull_bar = bars + 2 * STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* cload_bar = tempty_bar + 2;  // kNumCBuf entries (residual only)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cload_bar + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], kEpiThreads);
+    }
+    for (int i = 0; i < 4; ++i) mbar_init(&cload_bar[i], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (p.has_out_map) tma_prefetch_desc(&tmOut);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ----------------------------- TMA producer -----------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < s.tiles; tile += gridDim.x) {
+        const int m_blk = tile / s.n_blocks;
+        const int n_blk = tile - m_blk * s.n_blocks;
+        for (int kb = 0; kb < s.k_blocks; ++kb) {
+          if (!wait_parity(&empty_bar[stage], phase ^ 1u, kSiteProducerEmpty)) goto producer_done;
+          uint8_t* st = stage_base + stage * kStageBytes;
+          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+          tma_load_2d(st, &tmA, &full_bar[stage], kb * BK, m_blk * BM);
+          tma_load_2d(st + kTileABytes, &tmB, &full_bar[stage], kb * BK, n_blk * BN);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: do not leave the CTA while TMA writes into its shared memory are pending.
+      for (int i = 0; i < STAGES; ++i) {
+        if (!wait_parity(&empty_bar[stage], phase ^ 1u, kSiteDrain)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    producer_done:;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ----------------------------- MMA issuer -------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < s.tiles; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t tphase = (it >> 1) & 1;
+        if (!wait_parity(&tempty_bar[buf], tphase ^ 1u, kSiteMmaTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = 0; kb < s.k_blocks; ++kb) {
+          if (!wait_parity(&full_bar[stage], phase, kSiteMmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(stage_base + stage * kStageBytes);
+          const uint64_t a_desc = smem_desc_sw128(a_addr);
+          const uint64_t b_desc = smem_desc_sw128(a_addr + kTileABytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // Advance 16 bf16 (32 bytes) along K inside the swizzle atom: +2 in addr>>4.
+            mma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull_bar[buf]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------- Epilogue ---------------------------------
+    const int et = threadIdx.x - 64;  // 0..127
+    const int wq = warp & 3;          // TMEM lane quadrant this warp may access
+    const int r = wq * 32 + lane;     // accumulator row inside the tile
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+
+    if constexpr (KIND == kEpiAct) {
+      const uint32_t stg0 = smem_u32(epi_base);
+      int sbuf = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < s.tiles; tile += gridDim.x, ++it) {
+        const int m_blk = tile / s.n_blocks;
+        const int n_blk = tile - m_blk * s.n_blocks;
+        const int buf = it & 1;
+        const uint32_t tphase = (it >> 1) & 1;
+        {
+          const bool ok = wait_parity(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
+          if (named_bar_any(2, kEpiThreads, !ok)) break;
+        }
+        tc_fence_after();
+        const int row = m_blk * BM + r;
+        float mu = 0.f, rstd = 1.f;
+        const bool use_ln = p.ln.csum != nullptr;
+        if (use_ln && row < s.M) ln_row_stats(p.ln, row, mu, rstd);
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          const int n0 = n_blk * BN + c * 64;
+          float v[64];
+          const uint32_t ta = tmem_base + lane_off + buf * BN + c * 64;
+          tmem_ld32(ta, &v[0]);
+          tmem_ld32(ta + 32, &v[32]);
+          if (c == BN / 64 - 1) {
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[buf]);
+          }
+          if (n0 >= s.N) continue;  // uniform across the epilogue warps
+          if (use_ln) {
+            float cs[64];
+            load_vec64(p.ln.csum, n0, cs);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = rstd * fmaf(-mu, cs[j], v[j]);
+          }
+          if (p.vec != nullptr) {
+            float b[64];
+            load_vec64(p.vec, n0, b);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] += b[j];
+          }
+          if (p.act == 1) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = gelu_tanh(v[j]);
+          }
+          uint32_t w[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+          const uint32_t stg = stg0 + sbuf * 16384;
+          if (et == 0) bulk_wait_read<1>();
+          named_bar_sync(1, kEpiThreads);
+          stage_row_sw128(stg, r, w);
+          fence_proxy_async_smem();
+          named_bar_sync(1, kEpiThreads);
+          if (et == 0) {
+            tma_store_2d(&tmOut, epi_base + sbuf * 16384, n0, m_blk * BM);
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        }
+      }
+      if (et == 0) bulk_wait_all<0>();
+    } else if constexpr (KIND == kEpiNorm) {
+      const uint32_t stg0 = smem_u32(epi_base);
+      const int tiles_per_group = p.norm_width / BN;
+      const int part_cols = p.norm_groups * tiles_per_group;
+      int sbuf = 0;
+      int it = 0;
+      bool failed = false;
+      for (int tile = blockIdx.x; tile < s.tiles && !failed; tile += gridDim.x, ++it) {
+        const int m_blk = tile / s.n_blocks;
+        const int n_blk = tile - m_blk * s.n_blocks;
+        const int buf = it & 1;
+        const uint32_t tphase = (it >> 1) & 1;
+        {
+          const bool ok = wait_parity(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
+          if (named_bar_any(2, kEpiThreads, !ok)) break;
+        }
+        tc_fence_after();
+        const int row = m_blk * BM + r;
+        const bool row_ok = row < s.M;
+        float mu = 0.f, rstd = 1.f;
+        const bool use_ln = p.ln.csum != nullptr;
+        if (use_ln && row_ok) ln_row_stats(p.ln, row, mu, rstd);
+        const int group = (n_blk * BN) / p.norm_width;
+        const bool normed = group < p.norm_groups;
+        const uint32_t tbase = tmem_base + lane_off + buf * BN;
+        float rms = 1.f;
+        if (normed) {
+          // Pass 1: this tile's share of the row sum of squares (of the bf16-rounded
+          // projection, as WanRMSNorm sees the bf16 Linear output).
+          float ss = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; ++c) {
+            const int n0 = n_blk * BN + c * 64;
+            float v[64];
+            tmem_ld32(tbase + c * 64, &v[0]);
+            tmem_ld32(tbase + c * 64 + 32, &v[32]);
+            float b[64];
+            if (use_ln) {
+              load_vec64(p.ln.csum, n0, b);
+#pragma unroll
+              for (int j = 0; j < 64; ++j) v[j] = rstd * fmaf(-mu, b[j], v[j]);
+            }
+            if (p.vec != nullptr) {
+              load_vec64(p.vec, n0, b);
+#pragma unroll
+              for (int j = 0; j < 64; ++j) v[j] += b[j];
+            }
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              const float t = bf16_round(v[j]);
+              ss = fmaf(t, t, ss);
+            }
+          }
+          // Publish the partial, then wait for the other tiles of this (row block, group).
+          if (row_ok) p.part[static_cast<size_t>(row) * part_cols + n_blk] = ss;
+          __threadfence();
+          __syncwarp();
+          unsigned int* ctr = p.counters + m_blk * p.norm_groups + group;
+          const unsigned int target = 4u * tiles_per_group;
+          if (lane == 0) {
+            atomicAdd(ctr, 1u);
+            if (ld_acquire_gpu(ctr) < target) {
+              const uint64_t t0 = globaltimer_ns();
+              const uint64_t limit = g_wdit_wait_limit_ns;
+              while (ld_acquire_gpu(ctr) < target) {
+                if (globaltimer_ns() - t0 > limit) {
+                  report_error(kErrTimeout, kSiteExchange, static_cast<unsigned int>(tile));
+                  failed = true;
+                  break;
+                }
+                __nanosleep(64);
+              }
+            }
+          }
+          failed = named_bar_any(2, kEpiThreads, failed);
+          __threadfence();
+          float tot = 0.f;
+          if (row_ok) {
+            const float* pr = p.part + static_cast<size_t>(row) * part_cols + group * tiles_per_group;
+            for (int t = 0; t < tiles_per_group; ++t) tot += ld_cg_f32(pr + t);
+          }
+          rms = rsqrtf(tot / static_cast<float>(p.norm_width) + p.norm_eps);
+          __syncwarp();
+          if (lane == 0 && !failed) {
+            // Second round of arrivals: the last reader resets the counter for the next launch.
+            const unsigned int old = atomicAdd(ctr, 1u);
+            if (old == 2u * target - 1u) atomicExch(ctr, 0u);
+          }
+        }
+        const bool do_rope = normed && group < p.rope_groups;
+        const float* wn = normed ? p.norm_w[group] : nullptr;
+        int tok = 0;
+        if (do_rope && row_ok) {
+          const int b = row / p.rows_per_batch;
+          tok = row - b * p.rows_per_batch + p.token_offset;
+        }
+        // Pass 2 (pass 1 for plain columns): finish and store.
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          const int n0 = n_blk * BN + c * 64;
+          float v[64];
+          tmem_ld32(tbase + c * 64, &v[0]);
+          tmem_ld32(tbase + c * 64 + 32, &v[32]);
+          if (c == BN / 64 - 1) {
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[buf]);
+          }
+          if (n0 >= s.N) continue;
+          float b[64];
+          if (use_ln) {
+            load_vec64(p.ln.csum, n0, b);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = rstd * fmaf(-mu, b[j], v[j]);
+          }
+          if (p.vec != nullptr) {
+            load_vec64(p.vec, n0, b);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] += b[j];
+          }
+          if (normed) {
+            load_vec64(wn, n0 - group * p.norm_width, b);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              // WanRMSNorm rounding: bf16(bf16(x * rstd) * w), x the bf16 projection.
+              const float y = bf16_round(bf16_round(v[j]) * rms);
+              v[j] = bf16_round(y * b[j]);
+            }
+          }
+          if (do_rope) {
+            // Interleaved pairs (2i, 2i+1) of each 128-wide head rotated by the
+            // token's table entry i (44/42/42 frame/height/width split baked into the table).
+            const int pair0 = ((n0 - group * p.norm_width) & 127) >> 1;  // 0 or 32
+            float cs[32], sn[32];
+            if (row_ok) {
+              const float4* pc = reinterpret_cast<const float4*>(p.rope_cos + static_cast<size_t>(tok) * 64 + pair0);
+              const float4* ps = reinterpret_cast<const float4*>(p.rope_sin + static_cast<size_t>(tok) * 64 + pair0);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 a = __ldg(pc + q);
+                const float4 d = __ldg(ps + q);
+                cs[4 * q] = a.x; cs[4 * q + 1] = a.y; cs[4 * q + 2] = a.z; cs[4 * q + 3] = a.w;
+                sn[4 * q] = d.x; sn[4 * q + 1] = d.y; sn[4 * q + 2] = d.z; sn[4 * q + 3] = d.w;
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < 32; ++q) { cs[q] = 1.f; sn[q] = 0.f; }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float e = v[2 * i], o = v[2 * i + 1];
+              v[2 * i] = e * cs[i] - o * sn[i];
+              v[2 * i + 1] = e * sn[i] + o * cs[i];
+            }
+          }
+          uint32_t w[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+          const uint32_t stg = stg0 + sbuf * 16384;
+          if (et == 0) bulk_wait_read<1>();
+          named_bar_sync(1, kEpiThreads);
+          stage_row_sw128(stg, r, w);
+          fence_proxy_async_smem();
+          named_bar_sync(1, kEpiThreads);
+          if (et == 0) {
+            tma_store_2d(&tmOut, epi_base + sbuf * 16384, n0, m_blk * BM);
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        }
+      }
+      if (et == 0) bulk_wait_all<0>();
+    } else {
+      // ----------------------------- residual -----------------------------
+      constexpr int NB = Cfg<kEpiResidual>::kNumCBuf;
+      constexpr int CPT = BN / 32;  // 32-column chunks per tile
+      uint8_t* cbuf0 = epi_base;
+      uint8_t* xbuf0 = epi_base + NB * 16384;
+      const int my_tiles = (blockIdx.x < s.tiles) ? (s.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      const int total_chunks = my_tiles * CPT;
+      const bool has_x = p.has_x_map;
+      // Chunk g -> (tile, column chunk); issue the residual load of chunk g.
+      auto issue_load = [&](int g) {
+        const int ti = g / CPT;
+        const int c = g - ti * CPT;
+        const int tile = blockIdx.x + ti * gridDim.x;
+        const int m_blk = tile / s.n_blocks;
+        const int n_blk = tile - m_blk * s.n_blocks;
+        const int n0 = n_blk * BN + c * 32;
+        uint64_t* bar = &cload_bar[g % NB];
+        mbar_arrive_expect_tx(bar, 16384);
+        tma_load_2d(cbuf0 + (g % NB) * 16384, &tmC, bar, n0 < s.N ? n0 : 0, m_blk * BM);
+      };
+      if (et == 0) {
+        for (int g = 0; g < 2 && g < total_chunks; ++g) issue_load(g);
+      }
+      int g = 0;
+      bool failed = false;
+      for (int ti = 0; ti < my_tiles && !failed; ++ti) {
+        const int tile = blockIdx.x + ti * gridDim.x;
+        const int m_blk = tile / s.n_blocks;
+        const int n_blk = tile - m_blk * s.n_blocks;
+        const int buf = ti & 1;
+        const uint32_t tphase = (ti >> 1) & 1;
+        {
+          const bool ok = wait_parity(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
+          if (named_bar_any(2, kEpiThreads, !ok)) break;
+        }
+        tc_fence_after();
+        const int row = m_blk * BM + r;
+        const int batch = (row < s.M ? row : s.M - 1) / p.rows_per_batch;
+        const float* gb = p.gate_b != nullptr ? p.gate_b + static_cast<size_t>(batch) * p.gate_b_stride : nullptr;
+        float run_n = 0.f, run_mean = 0.f, run_m2 = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < CPT; ++c, ++g) {
+          const int n0 = n_blk * BN + c * 32;
+          if (et == 0) {
+            bulk_wait_read<1>();
+            if (g + 2 < total_chunks) issue_load(g + 2);
+          }
+          named_bar_sync(1, kEpiThreads);
+          float acc[32];
+          tmem_ld32(tmem_base + lane_off + buf * BN + c * 32, acc);
+          if (c == CPT - 1) {
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[buf]);
+          }
+          const bool c_ok = wait_parity(&cload_bar[g % NB], (g / NB) & 1, kSiteEpiCLoad);
+          const bool col_ok = n0 < s.N;
+          const uint32_t crow = smem_u32(cbuf0 + (g % NB) * 16384) + r * 128;
+          float out[32];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            ld_shared_v4(crow + ((q ^ (r & 7)) << 4), out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+          }
+          if (col_ok) {
+            const float4* bp = reinterpret_cast<const float4*>(p.vec + n0);
+            const float4* gp = p.gate_a != nullptr ? reinterpret_cast<const float4*>(p.gate_a + n0) : nullptr;
+            const float4* gbp = gb != nullptr ? reinterpret_cast<const float4*>(gb + n0) : nullptr;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float bb[4] = {0.f, 0.f, 0.f, 0.f};
+              if (p.vec != nullptr) {
+                const float4 t = __ldg(bp + q);
+                bb[0] = t.x; bb[1] = t.y; bb[2] = t.z; bb[3] = t.w;
+              }
+              if (gp != nullptr) {
+                const float4 t = __ldg(gp + q);
+                float gg[4] = {t.x, t.y, t.z, t.w};
+                if (gbp != nullptr) {
+                  const float4 u = __ldg(gbp + q);
+                  gg[0] += u.x; gg[1] += u.y; gg[2] += u.z; gg[3] += u.w;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) out[4 * q + j] = fmaf(acc[4 * q + j] + bb[j], gg[j], out[4 * q + j]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) out[4 * q + j] += acc[4 * q + j] + bb[j];
+              }
+            }
+          }
+          // Write the result back in place (same swizzled slots) for the TMA store.
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            st_shared_v4(crow + ((q ^ (r & 7)) << 4), __float_as_uint(out[4 * q]), __float_as_uint(out[4 * q + 1]),
+                         __float_as_uint(out[4 * q + 2]), __float_as_uint(out[4 * q + 3]));
+          }
+          if (col_ok && p.stats_out != nullptr) {
+            // Chunk (mean, M2), merged into the running per-row statistics (Chan).
+            float sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum += out[j];
+            const float cmean = sum * (1.f / 32.f);
+            float cm2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float d = out[j] - cmean;
+              cm2 = fmaf(d, d, cm2);
+            }
+            const float tot = run_n + 32.f;
+            const float delta = cmean - run_mean;
+            run_mean += delta * (32.f / tot);
+            run_m2 += cm2 + delta * delta * (run_n * 32.f / tot);
+            run_n = tot;
+          }
+          const uint32_t xrow = smem_u32(xbuf0 + (g & 1) * 8192) + r * 64;
+          if (has_x) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              st_shared_v4(xrow + ((q ^ ((r >> 1) & 3)) << 4), pack_bf16x2(out[8 * q], out[8 * q + 1]),
+                           pack_bf16x2(out[8 * q + 2], out[8 * q + 3]), pack_bf16x2(out[8 * q + 4], out[8 * q + 5]),
+                           pack_bf16x2(out[8 * q + 6], out[8 * q + 7]));
+            }
+          }
+          fence_proxy_async_smem();
+          if (named_bar_any(1, kEpiThreads, !c_ok)) {
+            failed = true;
+            break;
+          }
+          if (et == 0) {
+            if (col_ok) {
+              tma_store_2d(&tmOut, cbuf0 + (g % NB) * 16384, n0, m_blk * BM);
+              if (has_x) tma_store_2d(&tmX, xbuf0 + (g & 1) * 8192, n0, m_blk * BM);
+            }
+            bulk_commit();
+          }
+        }
+        if (!failed && p.stats_out != nullptr && row < s.M) {
+          const int ntiles = (s.N + BN - 1) / BN;
+          *reinterpret_cast<float2*>(p.stats_out + (static_cast<size_t>(row) * ntiles + n_blk) * 2) =
+              make_float2(run_mean, run_m2);
+        }
+      }
+      if (et == 0) bulk_wait_all<0>();
+      // Do not leave with residual loads in flight (only reachable after a failure).
+      if (failed && et == 0) {
+        for (int gg = g; gg <= g + 2 && gg < total_chunks; ++gg) wait_parity(&cload_bar[gg % NB], (gg / NB) & 1, kSiteDrain);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool get_encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  return g_encode != nullptr;
+}
+
+int make_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* ptr, int inner, int outer,
+             long long row_stride_elems, int box_inner, int box_outer, CUtensorMapSwizzle sw) {
+  if (!get_encoder()) return WDIT_ERR_DRIVER;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return WDIT_ERR_ALIGN;
+  if (((row_stride_elems * esize) & 15) != 0) return WDIT_ERR_ALIGN;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_elems * esize)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? WDIT_OK : WDIT_ERR_TMAP;
+}
+
+int g_num_sms = 0;
+
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return g_num_sms;
+}
+
+template <int KIND>
+int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const CUtensorMap& c,
+           const CUtensorMap& x, const GemmShape& s, const EpiParams& p, cudaStream_t stream, bool cooperative,
+           int max_ctas, int min_grid = 1) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  constexpr uint32_t smem = smem_bytes<KIND>();
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+    attr_set[dev & 63] = true;
+  }
+  int grid = num_sms();
+  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
+  if (s.tiles < grid) grid = s.tiles;
+  if (grid <= 0) return WDIT_OK;
+  // The cross-tile exchange of the norm epilogue needs the tiles of one group on distinct,
+  // co-resident CTAs: a grid smaller than the group would wait on its own later tile.
+  if (grid < min_grid) return WDIT_ERR_ARG;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = cooperative ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<KIND>, a, b, o, c, x, s, p);
+  return e == cudaSuccess ? WDIT_OK : WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+}
+
+int check_common(const void* A, int lda, const void* B, int ldb, int M, int N, int K) {
+  if (A == nullptr || B == nullptr) return WDIT_ERR_ARG;
+  if (M <= 0 || N <= 0 || K <= 0) return WDIT_ERR_SHAPE;
+  if (N % 64 != 0 || K % 8 != 0) return WDIT_ERR_SHAPE;
+  if (lda < K || ldb < K) return WDIT_ERR_SHAPE;
+  return WDIT_OK;
+}
+
+GemmShape make_shape(int M, int N, int K) {
+  GemmShape s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.m_blocks = (M + BM - 1) / BM;
+  s.n_blocks = (N + BN - 1) / BN;
+  s.k_blocks = (K + BK - 1) / BK;
+  s.tiles = s.m_blocks * s.n_blocks;
+  return s;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int build_ab(CUtensorMap* ma, CUtensorMap* mb, const void* A, int lda, const void* B, int ldb, int M, int N, int K) {
+  int rc = make_map(ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, K, M, lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  return make_map(mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, K, N, ldb, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int ln_fill(LnFold* ln, const float* csum, const float* stats, int stats_tiles, int stats_width, int row_len,
+            float eps) {
+  ln->csum = csum;
+  ln->stats = stats;
+  ln->stats_tiles = stats_tiles;
+  ln->stats_width = stats_width;
+  ln->row_len = row_len;
+  ln->eps = eps;
+  if (csum != nullptr) {
+    if (stats == nullptr || stats_tiles <= 0 || stats_width <= 0 || row_len <= 0) return WDIT_ERR_ARG;
+    if (!aligned16(csum) || (reinterpret_cast<uintptr_t>(stats) & 7) != 0) return WDIT_ERR_ALIGN;
+  }
+  return WDIT_OK;
+}
+
+}  // namespace
+}  // namespace wdit
+
+using namespace wdit;
+
+extern "C" {
+
+int wdit_stats_tile_width(void) { return BN; }
+
+int wdit_num_sms(void) { return num_sms(); }
+
+int wdit_set_wait_limit_ns(unsigned long long ns) {
+  cudaError_t e = cudaMemcpyToSymbol(g_wdit_wait_limit_ns, &ns, sizeof(ns));
+  return e == cudaSuccess ? WDIT_OK : WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+}
+
+int wdit_read_error(unsigned int* out4, int clear) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+  e = cudaMemcpyFromSymbol(out4, g_wdit_error, 4 * sizeof(unsigned int));
+  if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+  if (clear) {
+    unsigned int z[4] = {0, 0, 0, 0};
+    e = cudaMemcpyToSymbol(g_wdit_error, z, sizeof(z));
+    if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+  }
+  return WDIT_OK;
+}
+
+int wdit_gemm_act(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                  const float* vec, int act, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                  int ln_stats_width, float ln_eps, void* stream, int max_ctas) {
+  int rc = check_common(A, lda, B, ldb, M, N, K);
+  if (rc) return rc;
+  if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
+  if (act != 0 && act != 1) return WDIT_ERR_ARG;
+  if (vec != nullptr && !aligned16(vec)) return WDIT_ERR_ALIGN;
+  EpiParams p = {};
+  rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
+  if (rc) return rc;
+  p.vec = vec;
+  p.act = act;
+  p.rows_per_batch = M;
+  p.has_out_map = 1;
+  CUtensorMap ma, mb, mo, none;
+  memset(&none, 0, sizeof(none));
+  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  return launch<kEpiAct>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), false,
+                         max_ctas);
+}
+
+int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const float* C, int ldc, float* out, int ldo,
+                       int M, int N, int K, const float* bias, const float* gate_a, const float* gate_b,
+                       int gate_b_stride, int rows_per_batch, void* x_bf16_out, int ldx, float* stats_out,
+                       void* stream, int max_ctas) {
+  int rc = check_common(A, lda, B, ldb, M, N, K);
+  if (rc) return rc;
+  if (C == nullptr || out == nullptr || ldc < N || ldo < N) return WDIT_ERR_ARG;
+  if (gate_b != nullptr && (gate_a == nullptr || rows_per_batch <= 0 || gate_b_stride < N)) return WDIT_ERR_ARG;
+  if ((bias && !aligned16(bias)) || (gate_a && !aligned16(gate_a)) || (gate_b && !aligned16(gate_b)))
+    return WDIT_ERR_ALIGN;
+  if (gate_b != nullptr && (gate_b_stride % 4) != 0) return WDIT_ERR_ALIGN;
+  if (x_bf16_out != nullptr && ldx < N) return WDIT_ERR_ARG;
+  if (stats_out != nullptr && (reinterpret_cast<uintptr_t>(stats_out) & 7) != 0) return WDIT_ERR_ALIGN;
+  // An in-place update must be exactly in place: every tile reads its residual before storing.
+  if (C != out) {
+    const char* c0 = reinterpret_cast<const char*>(C);
+    const char* c1 = c0 + (static_cast<size_t>(M - 1) * ldc + N) * 4;
+    const char* o0 = reinterpret_cast<const char*>(out);
+    const char* o1 = o0 + (static_cast<size_t>(M - 1) * ldo + N) * 4;
+    if (c0 < o1 && o0 < c1) return WDIT_ERR_ALIAS;
+  } else if (ldc != ldo) {
+    return WDIT_ERR_ALIAS;
+  }
+  EpiParams p = {};
+  p.vec = bias;
+  p.gate_a = gate_a;
+  p.gate_b = gate_b;
+  p.gate_b_stride = gate_b_stride;
+  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
+  p.stats_out = stats_out;
+  p.has_out_map = 1;
+  p.has_x_map = x_bf16_out != nullptr ? 1 : 0;
+  CUtensorMap ma, mb, mo, mc, mx;
+  memset(&mx, 0, sizeof(mx));
+  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, N, M, ldc, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if (x_bf16_out != nullptr &&
+      (rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x_bf16_out, N, M, ldx, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
+    return rc;
+  return launch<kEpiResidual>(ma, mb, mo, mc, mx, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), false,
+                              max_ctas);
+}
+
+long long wdit_gemm_norm_workspace_bytes(int M, int N, int norm_groups, int norm_width) {
+  if (M <= 0 || norm_groups <= 0 || norm_width <= 0) return 0;
+  const long long m_blocks = (M + BM - 1) / BM;
+  const long long part_cols = static_cast<long long>(norm_groups) * (norm_width / BN);
+  const long long part = ((static_cast<long long>(M) * part_cols * 4 + 255) / 256) * 256;
+  const long long ctr = ((m_blocks * norm_groups * 4 + 255) / 256) * 256;
+  (void)N;
+  return part + ctr;
+}
+
+int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                   const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                   int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
+                   const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos, const float* rope_sin,
+                   int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes, void* stream,
+                   int max_ctas) {
+  int rc = check_common(A, lda, B, ldb, M, N, K);
+  if (rc) return rc;
+  if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
+  if (norm_groups < 0 || norm_groups > 2 || rope_groups < 0 || rope_groups > norm_groups) return WDIT_ERR_ARG;
+  if (norm_groups > 0) {
+    if (norm_width <= 0 || norm_width % BN != 0 || norm_groups * norm_width > N) return WDIT_ERR_SHAPE;
+    if (norm_w0 == nullptr || (norm_groups > 1 && norm_w1 == nullptr)) return WDIT_ERR_ARG;
+    if (!aligned16(norm_w0) || (norm_w1 && !aligned16(norm_w1))) return WDIT_ERR_ALIGN;
+    if (workspace == nullptr || workspace_bytes < wdit_gemm_norm_workspace_bytes(M, N, norm_groups, norm_width))
+      return WDIT_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return WDIT_ERR_ALIGN;
+  }
+  if (rope_groups > 0) {
+    if (rope_cos == nullptr || rope_sin == nullptr || rows_per_batch <= 0 || token_offset < 0) return WDIT_ERR_ARG;
+    if (!aligned16(rope_cos) || !aligned16(rope_sin)) return WDIT_ERR_ALIGN;
+    if (norm_width % 128 != 0) return WDIT_ERR_SHAPE;
+  }
+  if (vec != nullptr && !aligned16(vec)) return WDIT_ERR_ALIGN;
+  EpiParams p = {};
+  rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
+  if (rc) return rc;
+  p.vec = vec;
+  p.norm_groups = norm_groups;
+  p.norm_width = norm_groups > 0 ? norm_width : BN;
+  p.norm_w[0] = norm_w0;
+  p.norm_w[1] = norm_w1;
+  p.norm_eps = norm_eps;
+  p.rope_groups = rope_groups;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
+  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
+  p.token_offset = token_offset;
+  p.has_out_map = 1;
+  if (norm_groups > 0) {
+    const long long part_cols = static_cast<long long>(norm_groups) * (norm_width / BN);
+    const long long part = ((static_cast<long long>(M) * part_cols * 4 + 255) / 256) * 256;
+    p.part = reinterpret_cast<float*>(workspace);
+    p.counters = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(workspace) + part);
+  }
+  CUtensorMap ma, mb, mo, none;
+  memset(&none, 0, sizeof(none));
+  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  return launch<kEpiNorm>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
+                          norm_groups > 0, max_ctas, norm_groups > 0 ? norm_width / BN : 1);
+}
+
+}  // extern "C"

@@ -1,0 +1,294 @@
+"""Wan2.1 DiT forward on the fused blocks (single GPU or token-sharded over P GPUs).
+
+``FusedWanModel(model)`` takes a model with the stock WanModel attribute layout
+(``patch_embedding``, ``text_embedding``, ``time_embedding``, ``time_projection``,
+``blocks``, ``head.{head, modulation}``, ``freqs``) and installs ``FusedWanBlock`` for every
+block, as the reference does with ``model.blocks = ModuleList([CodaFullBlock(...)])``
+(coda_wan/run_wan_coda.py:254-263). ``forward(x_list, t, context_list, seq_len)`` keeps the
+stock call signature.
+
+``build_wan(cfg, seed, device)`` creates a randomly initialised model with that layout
+(Linear / conv weights ~N(0, 0.02), biases ~N(0, 0.01), modulation ~N(0,1)/sqrt(dim)); there
+is no checkpoint here. The non-block parts (patch embedding, text / time embeddings, head,
+unpatchify) run as small bf16 / fp32 ops around the blocks; the text MLP and the head use
+the fused GEMMs.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .block import Carry, FusedWanBlock
+from .ulysses import SeqParallel
+
+
+@dataclass(frozen=True)
+class WanShape:
+    dim: int = 1536
+    ffn_dim: int = 8960
+    num_heads: int = 12
+    num_layers: int = 30
+    freq_dim: int = 256
+    text_dim: int = 4096
+    text_len: int = 512
+    in_dim: int = 16
+    out_dim: int = 16
+    patch: tuple = (1, 2, 2)
+    eps: float = 1e-6
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.num_heads
+
+
+WAN_1_3B = WanShape()
+WAN_14B = WanShape(dim=5120, ffn_dim=13824, num_heads=40, num_layers=40)
+
+
+# ---------------------------------------------------------------------------
+# Parameter containers with the stock attribute layout (no forward of their own)
+# ---------------------------------------------------------------------------
+class _RMSNormParams(nn.Module):
+    def __init__(self, dim, eps):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+
+class _LayerNormParams(nn.Module):
+    def __init__(self, dim, eps, affine):
+        super().__init__()
+        self.eps = eps
+        if affine:
+            self.weight = nn.Parameter(torch.ones(dim))
+            self.bias = nn.Parameter(torch.zeros(dim))
+        else:
+            self.register_parameter("weight", None)
+            self.register_parameter("bias", None)
+
+
+class _AttentionParams(nn.Module):
+    def __init__(self, dim, num_heads, eps):
+        super().__init__()
+        self.num_heads = num_heads
+        self.eps = eps
+        self.window_size = (-1, -1)
+        self.q = nn.Linear(dim, dim)
+        self.k = nn.Linear(dim, dim)
+        self.v = nn.Linear(dim, dim)
+        self.o = nn.Linear(dim, dim)
+        self.norm_q = _RMSNormParams(dim, eps)
+        self.norm_k = _RMSNormParams(dim, eps)
+
+
+class WanBlockParams(nn.Module):
+    def __init__(self, s: WanShape):
+        super().__init__()
+        self.dim = s.dim
+        self.num_heads = s.num_heads
+        self.window_size = (-1, -1)
+        self.eps = s.eps
+        self.norm1 = _LayerNormParams(s.dim, s.eps, False)
+        self.self_attn = _AttentionParams(s.dim, s.num_heads, s.eps)
+        self.norm3 = _LayerNormParams(s.dim, s.eps, True)
+        self.cross_attn = _AttentionParams(s.dim, s.num_heads, s.eps)
+        self.norm2 = _LayerNormParams(s.dim, s.eps, False)
+        self.ffn = nn.Sequential(nn.Linear(s.dim, s.ffn_dim), nn.GELU(approximate="tanh"), nn.Linear(s.ffn_dim, s.dim))
+        self.modulation = nn.Parameter(torch.zeros(1, 6, s.dim))
+
+
+class _HeadParams(nn.Module):
+    def __init__(self, s: WanShape):
+        super().__init__()
+        self.norm = _LayerNormParams(s.dim, s.eps, False)
+        self.head = nn.Linear(s.dim, math.prod(s.patch) * s.out_dim)
+        self.modulation = nn.Parameter(torch.zeros(1, 2, s.dim))
+
+
+def rope_freqs(max_pos: int, head_dim: int, theta: float = 10000.0) -> torch.Tensor:
+    """complex128 [max_pos, head_dim/2] rotary frequencies, the head dimension split
+    d - 4(d//6), 2(d//6), 2(d//6) = 44/42/42 between frame, height and width."""
+    d = head_dim
+    cols = []
+    for n in (d - 4 * (d // 6), 2 * (d // 6), 2 * (d // 6)):
+        expo = torch.arange(0, n, 2, dtype=torch.float64) / n
+        ang = torch.outer(torch.arange(max_pos, dtype=torch.float64), torch.pow(theta, -expo))
+        cols.append(torch.polar(torch.ones_like(ang), ang))
+    return torch.cat(cols, dim=1)
+
+
+class WanParams(nn.Module):
+    def __init__(self, s: WanShape = WAN_1_3B, num_layers: int | None = None):
+        super().__init__()
+        self.cfg = s
+        self.dim = s.dim
+        self.num_heads = s.num_heads
+        self.patch_embedding = nn.Conv3d(s.in_dim, s.dim, kernel_size=s.patch, stride=s.patch)
+        self.text_embedding = nn.Sequential(nn.Linear(s.text_dim, s.dim), nn.GELU(approximate="tanh"),
+                                            nn.Linear(s.dim, s.dim))
+        self.time_embedding = nn.Sequential(nn.Linear(s.freq_dim, s.dim), nn.SiLU(), nn.Linear(s.dim, s.dim))
+        self.time_projection = nn.Sequential(nn.SiLU(), nn.Linear(s.dim, 6 * s.dim))
+        n = s.num_layers if num_layers is None else num_layers
+        self.blocks = nn.ModuleList([WanBlockParams(s) for _ in range(n)])
+        self.head = _HeadParams(s)
+        self.register_buffer("freqs", rope_freqs(1024, s.head_dim), persistent=False)
+
+
+def init_random_(module: nn.Module, seed: int) -> nn.Module:
+    """Seeded random init: weights ~N(0, 0.02), biases ~N(0, 0.01), modulation ~N(0,1)/sqrt(dim),
+    norm weights 1 and biases 0."""
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for name, p in module.named_parameters():
+            leaf = name.rsplit(".", 1)[-1]
+            if "modulation" in name:
+                p.copy_(torch.randn(p.shape, generator=g) / p.shape[-1] ** 0.5)
+            elif "norm" in name:
+                p.fill_(1.0 if leaf == "weight" else 0.0)
+            elif leaf == "weight":
+                p.copy_(0.02 * torch.randn(p.shape, generator=g))
+            else:
+                p.copy_(0.01 * torch.randn(p.shape, generator=g))
+    return module
+
+
+def build_wan(s: WanShape = WAN_1_3B, seed: int = 0, device="cuda", num_layers: int | None = None) -> WanParams:
+    """Random-init model with the stock layout, bf16 weights (time embedding / projection and
+    the modulation vectors fp32, as the stock model keeps them)."""
+    m = init_random_(WanParams(s, num_layers), seed)
+    m = m.to(device=device, dtype=torch.bfloat16)
+    m.time_embedding.float()
+    m.time_projection.float()
+    for blk in m.blocks:
+        blk.modulation.data = blk.modulation.data.float()
+    m.head.modulation.data = m.head.modulation.data.float()
+    m.freqs = rope_freqs(1024, s.head_dim).to(device)
+    return m
+
+
+def sinusoidal_embedding(dim: int, pos: torch.Tensor) -> torch.Tensor:
+    half = dim // 2
+    p = pos.to(torch.float64)
+    freq = torch.pow(10000.0, -torch.arange(half, dtype=torch.float64, device=p.device) / half)
+    s = torch.outer(p, freq)
+    return torch.cat([torch.cos(s), torch.sin(s)], dim=1)
+
+
+# ---------------------------------------------------------------------------
+# Fused model
+# ---------------------------------------------------------------------------
+class FusedWanModel(nn.Module):
+    def __init__(self, model: nn.Module, seq_parallel: SeqParallel | None = None):
+        super().__init__()
+        self.model = model
+        self.carry = Carry()
+        self.sp = seq_parallel
+        blocks = []
+        for b in model.blocks:
+            fb = b if isinstance(b, FusedWanBlock) else FusedWanBlock(b, carry=self.carry)
+            fb.carry = self.carry
+            fb.seq_parallel = seq_parallel
+            blocks.append(fb)
+        model.blocks = nn.ModuleList(blocks)
+        self.dim = int(model.patch_embedding.weight.shape[0])
+        self.patch = tuple(model.patch_embedding.kernel_size)
+        self.out_dim = model.head.head.weight.shape[0] // math.prod(self.patch)
+        self.freq_dim = model.time_embedding[0].weight.shape[1]
+        te = model.text_embedding
+        self.w_t1 = te[0].weight.detach().to(torch.bfloat16)
+        self.b_t1 = te[0].bias.detach().float()
+        self.w_t2 = te[2].weight.detach().to(torch.bfloat16)
+        self.b_t2 = te[2].bias.detach().float()
+        self.w_head = model.head.head.weight.detach().to(torch.bfloat16).contiguous()
+        self.b_head = model.head.head.bias.detach().float()
+        self.head_mod = model.head.modulation.detach().float().reshape(2, self.dim).contiguous()
+        self.eps = float(getattr(model.head.norm, "eps", 1e-6))
+
+    # -- embeddings --------------------------------------------------------
+    def embed_tokens(self, x_list, seq_len):
+        """Patch embedding -> [B, seq_len, dim] bf16 (zero-padded), grids, true lengths."""
+        pe = self.model.patch_embedding
+        w = pe.weight.to(torch.bfloat16)
+        b = pe.bias.to(torch.bfloat16)
+        xs = [F.conv3d(u.unsqueeze(0).to(torch.bfloat16), w, b, stride=self.patch) for u in x_list]
+        grids = [tuple(int(v) for v in u.shape[2:]) for u in xs]
+        xs = [u.flatten(2).transpose(1, 2) for u in xs]
+        lens = [u.shape[1] for u in xs]
+        x = torch.cat([F.pad(u, (0, 0, 0, seq_len - u.shape[1])) for u in xs])
+        return x, grids, lens
+
+    def embed_time(self, t: torch.Tensor):
+        e = self.model.time_embedding(sinusoidal_embedding(self.freq_dim, t).float())
+        e0 = self.model.time_projection(e).unflatten(1, (6, self.dim))
+        return e, e0
+
+    def embed_text(self, context_list, text_len):
+        ctx = torch.stack([F.pad(u.to(torch.bfloat16), (0, 0, 0, text_len - u.shape[0])) for u in context_list])
+        B, Lc, C = ctx.shape
+        c = ops.gemm_act(ctx.reshape(B * Lc, C), self.w_t1, vec=self.b_t1, act="gelu_tanh")
+        c = ops.gemm_act(c, self.w_t2, vec=self.b_t2, act="none")
+        return c.view(B, Lc, self.dim)
+
+    def head(self, x32, e, carry_stats, rows, shared_e: bool):
+        """LayerNorm + 2-vector modulation + Linear(dim -> prod(patch)*out_dim), LN absorbed."""
+        D = self.dim
+        xb, stats = carry_stats
+        e2 = e.float()
+        outs = []
+        Be = 1 if shared_e else e2.shape[0]
+        per = rows // Be
+        for b in range(Be):
+            r0, r1 = b * per, (b + 1) * per
+            wf, cs, vec = ops.fold_weight(self.w_head, mult_c=1.0, mult_a=self.head_mod[1], mult_b=e2[b],
+                                          shift_a=self.head_mod[0], shift_b=e2[b], bias=self.b_head)
+            outs.append(ops.gemm_act(xb[r0:r1], wf, vec=vec, act="none", ln=ops.LnFold(cs, stats[r0:r1], self.eps)))
+        return torch.cat(outs) if len(outs) > 1 else outs[0]
+
+    def unpatchify(self, y, grids, lens, rows_per_batch):
+        pt, ph, pw = self.patch
+        c = self.out_dim
+        outs = []
+        for i, ((f, h, w), n) in enumerate(zip(grids, lens)):
+            u = y[i * rows_per_batch: i * rows_per_batch + n].view(f, h, w, pt, ph, pw, c)
+            u = torch.einsum("fhwpqrc->cfphqwr", u)
+            outs.append(u.reshape(c, f * pt, h * ph, w * pw))
+        return outs
+
+    # -- forward -----------------------------------------------------------
+    def forward(self, x_list, t, context_list, seq_len, text_len: int = 512):
+        dev = self.model.patch_embedding.weight.device
+        B = len(x_list)
+        t = torch.as_tensor(t).reshape(-1)
+        # CFG: entries that share the timestep share the modulation (one weight fold per block).
+        # The check reads host values (one sync if t lives on the device).
+        tv = t.tolist()
+        shared_e = all(v == tv[0] for v in tv)
+        t = t.to(dev)
+        x, grids, lens = self.embed_tokens(x_list, seq_len)
+        e, e0 = self.embed_time(t[:1] if shared_e else t)
+        context = self.embed_text(context_list, text_len)
+        sp = self.sp
+        if sp is not None:
+            Lp = sp.local_len
+            x = x[:, sp.token_offset:sp.token_offset + Lp]
+        Lx = x.shape[1]
+        seq_lens = torch.tensor(lens, dtype=torch.long) if sp is None else None
+        grid_sizes = torch.tensor(grids, dtype=torch.long)
+        if any(n != seq_len for n in lens):
+            seq_lens_arg = seq_lens
+        else:
+            seq_lens_arg = None
+        x = x.contiguous()
+        for blk in self.model.blocks:
+            x = blk(x, e0, seq_lens_arg, grid_sizes, self.model.freqs, context, None)
+        x32 = x.reshape(B * Lx, self.dim)
+        carried = self.carry.get(x32)
+        y = self.head(x32, e, carried, B * Lx, shared_e)
+        if sp is not None:
+            return y.view(B, Lx, -1)
+        return [u.float() for u in self.unpatchify(y, grids, lens, Lx)]

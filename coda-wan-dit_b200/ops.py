@@ -1,0 +1,398 @@
+"""Fused ops of the Wan2.1 DiT block's non-attention half, on the wdit sm_100a kernels.
+
+Two layers:
+
+* Low-level fused GEMMs (``gemm_act``, ``gemm_residual``, ``gemm_norm``) and memory-bound
+  passes (``ln_stats``, ``fold_weight``) with the full epilogue feature set; the drop-in
+  block uses these.
+* The reference op API, same names / argument meaning / assertions as
+  coda_wan/wan_coda_kernels.py and coda_wan/wan_gate_residual_coda.py:
+  ``layernorm_modulation_bf16``, ``linear_bias_gelu_fixed``, ``qk_linear_bias_partial_rms``,
+  ``qk_rms_rope_from_partials``, ``qk_coda_rms_rope``, ``rmsnorm_fused``,
+  ``build_wan_rope_table``, ``prepack_linear_inplace``, ``prepack_qk_inplace``,
+  ``replace_parameter_with_view``, ``unique_storage_bytes``,
+  ``linear_gate_bias_residual_fixed``, ``linear_bias_residual_fixed``.
+
+GEMM operand B is K-major ([N, K] = nn.Linear.weight). The reference passes ``b_kn`` (K, N);
+its transposed view ``b_kn.t()`` is exactly that when ``b_kn`` is ``weight.T`` (what
+``prepack_linear_inplace`` returns here). A contiguous (K, N) ``b_kn`` is transposed once.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from ._lib import call, ptr, stream_ptr
+
+DIM = 1536
+HEAD_DIM = 128
+RMS_BLOCK = 128
+STATS_WIDTH = 256  # columns per LayerNorm-statistics partial (the GEMM's N tile)
+
+_ACT = {"none": 0, "gelu_tanh": 1}
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("wdit ops run on CUDA tensors only (no CPU implementation)")
+
+
+def _f32vec(v: torch.Tensor | None) -> torch.Tensor | None:
+    if v is None:
+        return None
+    v = v.reshape(-1)
+    if v.dtype != torch.float32:
+        v = v.float()
+    return v.contiguous()
+
+
+def _rowmajor(t: torch.Tensor) -> torch.Tensor:
+    """2-D with unit column stride (any row stride)."""
+    assert t.dim() == 2
+    if t.stride(1) != 1 or t.stride(0) < t.shape[1]:
+        t = t.contiguous()
+    return t
+
+
+def _weight_nk(b_kn: torch.Tensor) -> torch.Tensor:
+    """(K, N) operand -> [N, K] K-contiguous view (copy only if b_kn is N-major)."""
+    w = b_kn.t()
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    return w
+
+
+def stats_tiles(D: int) -> int:
+    return (D + STATS_WIDTH - 1) // STATS_WIDTH
+
+
+# ---------------------------------------------------------------------------
+# Low-level fused GEMMs
+# ---------------------------------------------------------------------------
+class LnFold:
+    """Absorbed LayerNorm: rstd_m * (acc - mu_m * csum[n]); (mu, rstd) from stats partials."""
+
+    __slots__ = ("csum", "stats", "eps")
+
+    def __init__(self, csum: torch.Tensor, stats: torch.Tensor, eps: float):
+        self.csum = csum
+        self.stats = stats
+        self.eps = float(eps)
+
+
+def _ln_args(ln: LnFold | None, K: int):
+    if ln is None:
+        return (None, None, 0, 0, 0.0)
+    assert ln.csum.dtype == torch.float32 and ln.stats.dtype == torch.float32
+    return (ptr(ln.csum), ptr(ln.stats), stats_tiles(K), STATS_WIDTH, ln.eps)
+
+
+def gemm_act(a, w, *, vec=None, act="none", ln: LnFold | None = None, out=None, max_ctas=0):
+    """out[M,N] bf16 = act(LN(a @ w.T) + vec). a bf16 [M,K]; w bf16 [N,K]."""
+    _require_cuda(a, w)
+    a = _rowmajor(a)
+    M, K = a.shape
+    N = w.shape[0]
+    assert w.shape[1] == K and w.stride(1) == 1
+    assert a.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    vec = _f32vec(vec)
+    call(
+        "wdit_gemm_act",
+        ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(out), out.stride(0), M, N, K,
+        ptr(vec), _ACT[act], *_ln_args(ln, K), stream_ptr(), max_ctas,
+    )
+    return out
+
+
+def gemm_residual(a, w, c, *, out=None, bias=None, gate_a=None, gate_b=None, gate_b_stride=0,
+                  rows_per_batch=0, x_bf16_out=None, stats_out=None, max_ctas=0):
+    """out[M,N] fp32 = c + (a @ w.T + bias) * (gate_a + gate_b[batch]); out may be c.
+
+    gate_b is a raw [batches, gate_b_stride] fp32 view (per-batch modulation rows).
+    """
+    _require_cuda(a, w, c)
+    a = _rowmajor(a)
+    M, K = a.shape
+    N = w.shape[0]
+    assert w.shape[1] == K and w.stride(1) == 1
+    assert c.dtype == torch.float32 and c.shape == (M, N) and c.stride(1) == 1
+    if out is None:
+        out = torch.empty_like(c)
+    assert out.dtype == torch.float32 and out.shape == (M, N) and out.stride(1) == 1
+    call(
+        "wdit_gemm_residual",
+        ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(c), c.stride(0), ptr(out), out.stride(0), M, N, K,
+        ptr(_f32vec(bias)), ptr(gate_a), ptr(gate_b), gate_b_stride, rows_per_batch,
+        ptr(x_bf16_out), 0 if x_bf16_out is None else x_bf16_out.stride(0), ptr(stats_out),
+        stream_ptr(), max_ctas,
+    )
+    return out
+
+
+def norm_workspace(M: int, N: int, norm_groups: int, norm_width: int, device) -> torch.Tensor:
+    nbytes = int(_lib.load().wdit_gemm_norm_workspace_bytes(M, N, norm_groups, norm_width))
+    return torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+
+
+class Workspace:
+    """Grow-only scratch for gemm_norm (the arrival counters must start at zero; the kernel
+    leaves them at zero after every successful launch)."""
+
+    def __init__(self):
+        self.buf: torch.Tensor | None = None
+
+    def get(self, M, N, groups, width, device) -> torch.Tensor:
+        need = int(_lib.load().wdit_gemm_norm_workspace_bytes(M, N, groups, width))
+        if self.buf is None or self.buf.numel() < need or self.buf.device != torch.device(device):
+            self.buf = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
+        return self.buf
+
+    def reset(self) -> None:
+        if self.buf is not None:
+            self.buf.zero_()
+
+
+_default_ws: dict[int, Workspace] = {}
+
+
+def _ws_for(device) -> Workspace:
+    idx = torch.device(device).index or 0
+    if idx not in _default_ws:
+        _default_ws[idx] = Workspace()
+    return _default_ws[idx]
+
+
+def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_width=0, norm_w=(None, None),
+              norm_eps=1e-6, rope_groups=0, rope_cos=None, rope_sin=None, rows_per_batch=0, token_offset=0,
+              out=None, workspace: Workspace | None = None, max_ctas=0):
+    """out[M,N] bf16 = RoPE(RMSNorm_fullwidth(bf16(LN(a @ w.T) + vec))) per column group."""
+    _require_cuda(a, w)
+    a = _rowmajor(a)
+    M, K = a.shape
+    N = w.shape[0]
+    assert w.shape[1] == K and w.stride(1) == 1
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    ws = None
+    nbytes = 0
+    if norm_groups > 0:
+        ws = (workspace or _ws_for(a.device)).get(M, N, norm_groups, norm_width, a.device)
+        nbytes = ws.numel()
+    w0 = _f32vec(norm_w[0]) if norm_groups > 0 else None
+    w1 = _f32vec(norm_w[1]) if norm_groups > 1 else None
+    call(
+        "wdit_gemm_norm",
+        ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(out), out.stride(0), M, N, K,
+        ptr(_f32vec(vec)), *_ln_args(ln, K), norm_groups, norm_width, ptr(w0), ptr(w1), float(norm_eps),
+        rope_groups, ptr(rope_cos), ptr(rope_sin), rows_per_batch, token_offset, ptr(ws), nbytes,
+        stream_ptr(), max_ctas,
+    )
+    return out
+
+
+def ln_stats(x, *, stats_out=None, x_bf16_out=None, x_f32_out=None):
+    """Per-256-column (mean, M2) of the rows of x [M, D] (bf16 or fp32)."""
+    _require_cuda(x)
+    x = _rowmajor(x)
+    M, D = x.shape
+    if stats_out is None:
+        stats_out = torch.empty((M, stats_tiles(D), 2), dtype=torch.float32, device=x.device)
+    call(
+        "wdit_ln_stats",
+        ptr(x), 1 if x.dtype == torch.bfloat16 else 0, x.stride(0), M, D, ptr(stats_out), ptr(x_bf16_out),
+        ptr(x_f32_out), stream_ptr(),
+    )
+    return stats_out
+
+
+def fold_weight(w, *, mult_c, mult_a=None, mult_b=None, shift_a=None, shift_b=None, bias=None, w_out=None,
+                csum_out=None, vec_out=None):
+    """W'[n,k] = bf16(W[n,k] * (mult_c + mult_a[k] + mult_b[k])), csum = rowsum(W'),
+    vec[n] = sum_k (shift_a + shift_b)[k] W[n,k] + bias[n]."""
+    _require_cuda(w)
+    N, K = w.shape
+    assert w.stride(1) == 1 and w.dtype == torch.bfloat16
+    if w_out is None:
+        w_out = torch.empty((N, K), dtype=torch.bfloat16, device=w.device)
+    if csum_out is None:
+        csum_out = torch.empty(N, dtype=torch.float32, device=w.device)
+    if vec_out is None:
+        vec_out = torch.empty(N, dtype=torch.float32, device=w.device)
+    call(
+        "wdit_fold_weight",
+        ptr(w), w.stride(0), N, K, float(mult_c), ptr(mult_a), ptr(mult_b), ptr(shift_a), ptr(shift_b),
+        ptr(_f32vec(bias)), ptr(w_out), w_out.stride(0), ptr(csum_out), ptr(vec_out), stream_ptr(),
+    )
+    return w_out, csum_out, vec_out
+
+
+# ---------------------------------------------------------------------------
+# Reference op API (coda_wan/wan_coda_kernels.py, coda_wan/wan_gate_residual_coda.py)
+# ---------------------------------------------------------------------------
+def layernorm_modulation_bf16(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, eps: float) -> torch.Tensor:
+    """bf16(LN_noaffine(x) * (1 + scale) + shift).  wan_coda_kernels.py:59-81."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    assert x2.shape[1] == DIM
+    assert scale.numel() == shift.numel() == DIM
+    _require_cuda(x2)
+    x2 = _rowmajor(x2)
+    out = torch.empty((x2.shape[0], DIM), dtype=torch.bfloat16, device=x.device)
+    call(
+        "wdit_layernorm_modulation",
+        ptr(x2), 1 if x2.dtype == torch.bfloat16 else 0, x2.stride(0), x2.shape[0], DIM,
+        ptr(_f32vec(scale)), ptr(_f32vec(shift)), float(eps), ptr(out), DIM, stream_ptr(),
+    )
+    return out.view(shape)
+
+
+def linear_bias_gelu_fixed(a: torch.Tensor, b_kn: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """GELU-tanh(A @ B + bias) stored bf16.  wan_coda_kernels.py:120-152."""
+    assert a.ndim == b_kn.ndim == 2 and bias.ndim == 1
+    assert a.shape[1] == b_kn.shape[0] and b_kn.shape[1] == bias.shape[0]
+    return gemm_act(a, _weight_nk(b_kn), vec=bias, act="gelu_tanh")
+
+
+def qk_linear_bias_partial_rms(a, qk_weight_kn, qk_bias, block_size: int = RMS_BLOCK):
+    """[q|k] = A @ W + b (bf16) and per-128-column mean-square partials [M, 24].
+    wan_coda_kernels.py:192-230."""
+    m, k = a.shape
+    assert qk_weight_kn.shape == (k, 2 * DIM)
+    assert qk_bias.shape == (2 * DIM,)
+    assert (2 * DIM) % block_size == 0
+    qk = gemm_act(a, _weight_nk(qk_weight_kn), vec=qk_bias, act="none")
+    partial = torch.empty((m, 2 * DIM // block_size), dtype=torch.float32, device=a.device)
+    call("wdit_block_mean_sq", ptr(qk), qk.stride(0), m, 2 * DIM, block_size, ptr(partial), stream_ptr())
+    return qk, partial
+
+
+def qk_rms_rope_from_partials(qk, partial, q_weight, k_weight, cos, sin, eps):
+    """WanRMSNorm (full width, bf16 roundings) + interleaved 3D RoPE, in place over qk.
+    wan_coda_kernels.py:313-352."""
+    m = qk.shape[0]
+    assert qk.shape == (m, 2 * DIM)
+    parts = DIM // RMS_BLOCK
+    assert partial.shape == (m, 2 * parts)
+    assert cos.shape == sin.shape == (m, HEAD_DIM // 2)
+    _require_cuda(qk, partial, cos, sin)
+    assert qk.stride(1) == 1 and partial.is_contiguous()
+    call(
+        "wdit_qk_rms_rope_from_partials",
+        ptr(qk), qk.stride(0), ptr(partial), m, DIM, ptr(_f32vec(q_weight)), ptr(_f32vec(k_weight)),
+        ptr(cos.float().contiguous()), ptr(sin.float().contiguous()), float(eps), stream_ptr(),
+    )
+    return qk[:, :DIM], qk[:, DIM:]
+
+
+def qk_coda_rms_rope(a, qk_weight_kn, qk_bias, q_weight, k_weight, cos, sin, eps):
+    """One fused GEMM: q, k = RoPE(RMSNorm(A @ [Wq|Wk] + b)).  wan_coda_kernels.py:355-368.
+
+    cos/sin are [m, 64] per-row tables (row i = token i), as in the reference.
+    """
+    m, k = a.shape
+    assert qk_weight_kn.shape == (k, 2 * DIM)
+    assert qk_bias.shape == (2 * DIM,)
+    assert cos.shape == sin.shape == (m, HEAD_DIM // 2)
+    qk = gemm_norm(
+        a, _weight_nk(qk_weight_kn), vec=qk_bias, norm_groups=2, norm_width=DIM, norm_w=(q_weight, k_weight),
+        norm_eps=eps, rope_groups=2, rope_cos=cos.float().contiguous(), rope_sin=sin.float().contiguous(),
+        rows_per_batch=m, token_offset=0,
+    )
+    return qk[:, :DIM], qk[:, DIM:]
+
+
+def rmsnorm_fused(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w) over the full width.  wan_coda_kernels.py:392-411."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    assert x2.shape[1] == DIM
+    _require_cuda(x2)
+    x2 = _rowmajor(x2.to(torch.bfloat16) if x2.dtype != torch.bfloat16 else x2)
+    out = torch.empty((x2.shape[0], DIM), dtype=torch.bfloat16, device=x.device)
+    call("wdit_rmsnorm", ptr(x2), x2.stride(0), x2.shape[0], DIM, ptr(_f32vec(weight)), float(eps), ptr(out), DIM,
+         stream_ptr())
+    return out.view(shape)
+
+
+def build_wan_rope_table(grid_fhw, freqs: torch.Tensor):
+    """Shared per-token cos/sin [f*h*w, 64] fp32 tables.  wan_coda_kernels.py:414-430."""
+    f, h, w = (int(v) for v in grid_fhw)
+    _require_cuda(freqs)
+    assert freqs.dim() == 2 and freqs.shape[1] == HEAD_DIM // 2 and freqs.is_complex()
+    fr = torch.view_as_real(freqs.to(torch.complex128).contiguous()).contiguous()
+    cos = torch.empty((f * h * w, HEAD_DIM // 2), dtype=torch.float32, device=freqs.device)
+    sin = torch.empty_like(cos)
+    call("wdit_rope_table", ptr(fr), freqs.shape[0], f, h, w, ptr(cos), ptr(sin), stream_ptr())
+    return cos, sin
+
+
+def replace_parameter_with_view(module: nn.Module, name: str, view: torch.Tensor) -> None:
+    module._parameters[name] = nn.Parameter(view, requires_grad=False)
+
+
+def prepack_linear_inplace(linear: nn.Linear) -> torch.Tensor:
+    """(K, N) operand of a Linear with zero copies: the K-major weight is the GEMM's native
+    B layout, so the packed operand is a transposed view of the parameter's own storage.
+    Counterpart of wan_coda_kernels.py:441-445 (which needs a transpose copy for its GEMM)."""
+    return linear.weight.detach().T
+
+
+def prepack_qk_inplace(q: nn.Linear, k: nn.Linear):
+    """Pack Q and K into one [2N, K] allocation; the parameters become views of it.
+    wan_coda_kernels.py:448-461."""
+    packed = torch.cat([q.weight.detach(), k.weight.detach()], dim=0).contiguous()
+    bias = torch.cat([q.bias.detach(), k.bias.detach()]).contiguous()
+    n = q.weight.shape[0]
+    replace_parameter_with_view(q, "weight", packed[:n])
+    replace_parameter_with_view(k, "weight", packed[n:])
+    replace_parameter_with_view(q, "bias", bias[:n])
+    replace_parameter_with_view(k, "bias", bias[n:])
+    return packed.T, bias
+
+
+def prepack_qkv_inplace(q: nn.Linear, k: nn.Linear, v: nn.Linear):
+    """Q, K and V packed into one [3N, K] allocation (the fused QKV GEMM's B operand);
+    the three Linear parameters become views of it (no duplicate bytes)."""
+    packed = torch.cat([q.weight.detach(), k.weight.detach(), v.weight.detach()], dim=0).contiguous()
+    bias = torch.cat([q.bias.detach(), k.bias.detach(), v.bias.detach()]).contiguous()
+    n = q.weight.shape[0]
+    for i, lin in enumerate((q, k, v)):
+        replace_parameter_with_view(lin, "weight", packed[i * n:(i + 1) * n])
+        replace_parameter_with_view(lin, "bias", bias[i * n:(i + 1) * n])
+    return packed, bias
+
+
+def unique_storage_bytes(module: nn.Module, extras: list[torch.Tensor]) -> int:
+    """Unique CUDA storage bytes across parameters, buffers and extras.  wan_coda_kernels.py:464-477."""
+    seen: set[tuple[int, int]] = set()
+    total = 0
+    for tensor in list(module.parameters()) + list(module.buffers()) + list(extras):
+        if tensor.device.type != "cuda":
+            continue
+        storage = tensor.untyped_storage()
+        key = (storage.data_ptr(), storage.nbytes())
+        if key not in seen:
+            seen.add(key)
+            total += storage.nbytes()
+    return total
+
+
+def linear_gate_bias_residual_fixed(A, B, C, gate, bias, *, inplace: bool = False):
+    """(A @ B) * gate + bias * gate + C in fp32; out may alias C.  wan_gate_residual_coda.py:192-242."""
+    assert gate.shape == bias.shape == (B.shape[1],)
+    assert A.ndim == B.ndim == C.ndim == 2
+    out = C if inplace else torch.empty_like(C)
+    return gemm_residual(A, _weight_nk(B), C, out=out, bias=bias, gate_a=_f32vec(gate))
+
+
+def linear_bias_residual_fixed(A, B, C, bias, *, inplace: bool = False):
+    """A @ B + bias + C in fp32; out may alias C.  wan_gate_residual_coda.py:99-135."""
+    assert A.ndim == B.ndim == C.ndim == 2
+    assert bias.shape == (B.shape[1],)
+    assert A.shape[0] == C.shape[0] and B.shape[1] == C.shape[1]
+    out = C if inplace else torch.empty_like(C)
+    return gemm_residual(A, _weight_nk(B), C, out=out, bias=bias)

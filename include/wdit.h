@@ -1,0 +1,193 @@
+/*
+ * wdit.h - C ABI of the B200 (sm_100a) kernels for the non-attention half of the
+ * Wan2.1 DiT block (library: coda-wan-dit_b200/libwdit.so).
+ *
+ * Conventions
+ *   - Plain device pointers, element counts / leading dimensions in ELEMENTS, and a
+ *     cudaStream_t passed as `void* stream` (NULL = legacy default stream).
+ *   - Matrices are row-major. GEMM operand B is the nn.Linear weight [N, K] (K contiguous),
+ *     i.e. the reference's `b_kn` (K, N) argument seen as a transposed view.
+ *   - bf16 tensors are `void*` (2-byte elements), fp32 tensors `float*`.
+ *   - Nothing here allocates device memory: the caller owns every buffer, including the
+ *     scratch workspace of wdit_gemm_norm (size from wdit_gemm_norm_workspace_bytes).
+ *   - Return value: 0 on success, a WDIT_ERR_* code otherwise (launch errors are
+ *     WDIT_ERR_CUDA_BASE + cudaError_t). Asynchronous device-side failures (a bounded
+ *     wait that ran out) are recorded on the device and read with wdit_read_error.
+ *   - Alignment: every pointer 16-byte aligned; leading dimensions a multiple of 16 bytes.
+ *   - N must be a multiple of 64 and K a multiple of 8 for the GEMMs; M is arbitrary.
+ *
+ * Each entry point names the reference (Owen718/CODA-Wan-DiT) interface it replaces.
+ */
+#ifndef WDIT_H_
+#define WDIT_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WDIT_OK 0
+#define WDIT_ERR_ARG 1        /* null pointer or inconsistent argument */
+#define WDIT_ERR_SHAPE 2      /* unsupported shape */
+#define WDIT_ERR_ALIGN 3      /* pointer / stride alignment */
+#define WDIT_ERR_ALIAS 4      /* partially overlapping in-place buffers */
+#define WDIT_ERR_WORKSPACE 5  /* workspace missing or too small */
+#define WDIT_ERR_TMAP 6       /* cuTensorMapEncodeTiled rejected a descriptor */
+#define WDIT_ERR_DRIVER 7     /* driver entry point unavailable */
+#define WDIT_ERR_CUDA_BASE 1000
+
+/* ---- runtime / diagnostics (no reference counterpart; the reference uses Python asserts) ---- */
+
+/* Number of SMs of the current device (the persistent grid size). */
+int wdit_num_sms(void);
+
+/* Make `device` current for this library's CUDA runtime in the calling thread (the library
+ * links its own runtime; callers keep it equal to their framework's current device). */
+int wdit_set_device(int device);
+
+/* Width (columns) of one LayerNorm-statistics partial written by wdit_gemm_residual. */
+int wdit_stats_tile_width(void);
+
+/* Upper bound, in nanoseconds, of every device-side wait (default 2 s). */
+int wdit_set_wait_limit_ns(unsigned long long ns);
+
+/* Synchronizes the device and copies the device error record
+ * {code, site, block, extra} into out4 (all zero = no error); clear != 0 resets it. */
+int wdit_read_error(unsigned int* out4, int clear);
+
+/* ---- fused GEMMs ---- */
+
+/*
+ * out[M,N] (bf16) = act( LN(A . B^T) + vec ),   act: 0 identity, 1 tanh-GELU.
+ * LN is the absorbed adaLN LayerNorm: rstd_m * (acc - mu_m * ln_csum[n]) where (mu, rstd) of
+ * row m are merged from ln_stats[m, 0..ln_stats_tiles-1] = (mean, M2) over ln_stats_width
+ * columns each (as written by wdit_gemm_residual / wdit_ln_stats); ln_csum = NULL disables it.
+ * Replaces: coda_wan/wan_coda_kernels.py:120-152 linear_bias_gelu_fixed (EVTGELUBias :84-105)
+ * together with the LN+modulate kernel it consumes (:35-81, removed by the fold).
+ */
+int wdit_gemm_act(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                  const float* vec, int act, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                  int ln_stats_width, float ln_eps, void* stream, int max_ctas);
+
+/*
+ * out[M,N] (fp32) = C + (A . B^T + bias) * gate,  gate[m, n] = gate_a[n] + gate_b[batch(m), n]
+ * (gate_a = NULL: no gate, out = C + A . B^T + bias). batch(m) = m / rows_per_batch.
+ * out may alias C exactly (in-place residual update). Optional side outputs:
+ * x_bf16_out[M,N] = bf16(out), stats_out[M, ceil(N/256), 2] = per-256-column (mean, M2) of out.
+ * Replaces: coda_wan/wan_gate_residual_coda.py:192-242 linear_gate_bias_residual_fixed and
+ * :99-135 linear_bias_residual_fixed.
+ */
+int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const float* C, int ldc, float* out, int ldo,
+                       int M, int N, int K, const float* bias, const float* gate_a, const float* gate_b,
+                       int gate_b_stride, int rows_per_batch, void* x_bf16_out, int ldx, float* stats_out,
+                       void* stream, int max_ctas);
+
+/* Workspace bytes wdit_gemm_norm needs (partials + arrival counters). The counter part must be
+ * zero before the first launch; the kernel leaves it zero after every successful launch. */
+long long wdit_gemm_norm_workspace_bytes(int M, int N, int norm_groups, int norm_width);
+
+/*
+ * out[M,N] (bf16): y = LN(A . B^T) + vec, rounded to bf16; columns [g*W, (g+1)*W) for
+ * g < norm_groups get the full-width WanRMSNorm bf16(bf16(y * rsqrt(mean_W(y^2) + eps)) * w_g),
+ * and for g < rope_groups the interleaved-pair 3D RoPE with rope_cos/sin[token, 64] where
+ * token = m % rows_per_batch + token_offset. Remaining columns are stored as bf16(y).
+ * QKV: norm_groups 2, rope_groups 2; cross-Q: 1, 0; cross-KV: 1, 0.
+ * Replaces: coda_wan/wan_coda_kernels.py:355-368 qk_coda_rms_rope (= :192-230
+ * qk_linear_bias_partial_rms + :313-352 qk_rms_rope_from_partials), the V projection at
+ * coda_wan/run_wan_coda.py:158, and :371-411 rmsnorm_fused applied to cross-attention q / k.
+ */
+int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                   const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                   int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
+                   const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos, const float* rope_sin,
+                   int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes, void* stream,
+                   int max_ctas);
+
+/* ---- memory-bound passes ---- */
+
+/*
+ * Row statistics of x[M,D] (x_is_bf16 selects bf16 or fp32 input) in the format of
+ * wdit_gemm_residual's stats_out (per-256-column (mean, M2)); optionally writes bf16(x) and
+ * fp32(x). The stats pass for the first block, whose input no residual epilogue produced.
+ * Replaces: the statistics half of coda_wan/wan_coda_kernels.py:35-56 (_layernorm_modulation_kernel).
+ */
+int wdit_ln_stats(const void* x, int x_is_bf16, int ldx, int M, int D, float* stats_out, void* x_bf16_out,
+                  float* x_f32_out, void* stream);
+
+/*
+ * Per-step weight fold of an adaLN LayerNorm into the following Linear W[N,K] (bf16):
+ *   mult[k]  = mult_c + mult_a[k] + mult_b[k]       (mult_b nullable)
+ *   shift[k] = shift_a[k] + shift_b[k]              (both nullable)
+ *   Wf[n,k]  = bf16(W[n,k] * mult[k]),  csum[n] = sum_k Wf[n,k],
+ *   vec[n]   = sum_k shift[k] * W[n,k] + bias[n]    (bias nullable)
+ * Modulation: mult_c = 1, mult_a = modulation[scale], mult_b = e[scale], shift = modulation[shift] + e[shift].
+ * Static norm3 fold: mult_c = 0, mult_a = gamma, shift_a = beta.
+ * Replaces: the modulation add at coda_wan/run_wan_coda.py:142 and the (1 + scale) / shift of
+ * coda_wan/wan_coda_kernels.py:52-55, moved from the activations to the weight.
+ */
+int wdit_fold_weight(const void* W, int ldw, int N, int K, float mult_c, const float* mult_a, const float* mult_b,
+                     const float* shift_a, const float* shift_b, const float* bias, void* W_out, int ldw_out,
+                     float* csum_out, float* vec_out, void* stream);
+
+/*
+ * out[M,D] (bf16) = (x - mean) * rsqrt(var + eps) * (1 + scale) + shift, x fp32 or bf16.
+ * Replaces: coda_wan/wan_coda_kernels.py:59-81 layernorm_modulation_bf16.
+ */
+int wdit_layernorm_modulation(const void* x, int x_is_bf16, int ldx, int M, int D, const float* scale,
+                              const float* shift, float eps, void* out, int ldo, void* stream);
+
+/*
+ * out[M,D] (bf16) = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w), x bf16.
+ * Replaces: coda_wan/wan_coda_kernels.py:392-411 rmsnorm_fused.
+ */
+int wdit_rmsnorm(const void* x, int ldx, int M, int D, const float* w, float eps, void* out, int ldo, void* stream);
+
+/*
+ * In-place WanRMSNorm + RoPE of q and k from per-128-column mean-square partials.
+ * qk[M, 2D] bf16, partial[M, 2D/128] fp32, wq/wk[D] fp32, cos/sin[M, 64] fp32.
+ * Replaces: coda_wan/wan_coda_kernels.py:313-352 qk_rms_rope_from_partials.
+ */
+int wdit_qk_rms_rope_from_partials(void* qk, int ldqk, const float* partial, int M, int D, const float* wq,
+                                   const float* wk, const float* cos_tab, const float* sin_tab, float eps,
+                                   void* stream);
+
+/*
+ * cos/sin[f*h*w, 64] (fp32) of the 3D RoPE for grid (f, h, w), from the per-axis complex
+ * frequency table freqs[max_pos, 64] (complex128 stored as interleaved fp64 (re, im) pairs);
+ * the 64 columns split [22, 21, 21] between the frame, height and width axes.
+ * Replaces: coda_wan/wan_coda_kernels.py:414-430 build_wan_rope_table.
+ */
+int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, float* cos_out, float* sin_out,
+                    void* stream);
+
+/*
+ * Mean of squares of x[M,N] (bf16) over consecutive column blocks: out[M, N/block] (fp32).
+ * Replaces: the partial output of coda_wan/wan_coda_kernels.py:192-230
+ * qk_linear_bias_partial_rms (EVTColBlockReductionStore with the mean-square op).
+ */
+int wdit_block_mean_sq(const void* x, int ldx, int M, int N, int block, float* out, void* stream);
+
+/* ---- sequence-parallel (Ulysses) regrouping; no reference counterpart (the reference is
+ * single-GPU), these serve the token-sharded multi-GPU forward ----
+ * Units: u = b*H + h over the B*H (batch, head) pairs, U = B*H/P units per rank, unit u on
+ * rank u / U. Rank r owns tokens [r*Lp, (r+1)*Lp) of every batch entry. hd % 8 == 0.
+ */
+
+/* send[P][nmat][U][Lp][hd] <- src rows (b*Lp + t), columns (c*H + h)*hd + i, c < nmat. */
+int wdit_ulysses_pack(const void* src, int ld, int B, int Lp, int H, int hd, int nmat, int P, void* send,
+                      void* stream);
+
+/* dst[nmat][U][P*Lp][hd] <- recv[P][nmat][U][Lp][hd] (full sequence per unit). */
+int wdit_seq_gather(const void* recv, int nmat, int U, int P, int Lp, int hd, void* dst, void* stream);
+
+/* send[P][U][Lp][hd] <- o[j*unit_stride + token*tok_stride + i] (attention output per unit). */
+int wdit_seq_scatter(const void* o, long long unit_stride, long long tok_stride, int U, int P, int Lp, int hd,
+                     void* send, void* stream);
+
+/* dst rows (b*Lp + t), columns h*hd + i <- recv[P][U][Lp][hd]. */
+int wdit_ulysses_unpack(const void* recv, int B, int Lp, int H, int hd, int P, void* dst, int ld, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WDIT_H_ */

@@ -1,0 +1,122 @@
+"""The drop-in block and the DiT forward against the stock-Wan oracle on the GPU.
+
+Tolerances from the target spec: block output relative L2 <= 1e-2 and max |diff| <= 5e-2
+(vs the stock eager block in bf16 mixed precision and vs the fp32 oracle); multi-layer
+output relative L2 <= 2e-2."""
+import pytest
+import torch
+
+from oracle import wan_ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_l2(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm()).item()
+
+
+def max_abs(a, b):
+    return (a.float() - b.float()).abs().max().item()
+
+
+@pytest.fixture(autouse=True)
+def _check_device_errors(pkg):
+    yield
+    pkg._lib.raise_on_device_error()
+
+
+def make_pair(pkg, seed=7, jitter=0.1, cfg=wan_ref.WAN_1_3B):
+    ref = wan_ref.init_weights_(wan_ref.WanBlockRef(cfg, torch.float32), seed=seed, norm_jitter=jitter).to(DEV)
+    inner = wan_ref.WanBlockRef(cfg, torch.float32).to(DEV)
+    inner.load_state_dict(ref.state_dict())
+    inner = inner.to(torch.bfloat16)
+    inner.modulation.data = inner.modulation.data.float()
+    stock = wan_ref.WanBlockRef(cfg, torch.bfloat16).to(DEV)
+    stock.load_state_dict(ref.state_dict())
+    return ref, stock, pkg.FusedWanBlock(inner)
+
+
+def run(blk, inp, freqs, x=None, e=None, ctx_dtype=None):
+    x = inp["x"].clone() if x is None else x
+    e = inp["e"] if e is None else e
+    ctx = inp["context"] if ctx_dtype is None else inp["context"].to(ctx_dtype)
+    with torch.no_grad():
+        return blk(x, e, inp["seq_lens"], inp["grid_sizes"], freqs, ctx, inp["context_lens"])
+
+
+@pytest.mark.parametrize("grid,batch", [((1, 30, 52), 1), ((2, 6, 10), 2)])
+def test_block_matches_stock_oracle(pkg, grid, batch):
+    ref, stock, fused = make_pair(pkg)
+    inp = wan_ref.block_inputs(wan_ref.WAN_1_3B, grid, batch, seed=11, device=DEV)
+    if batch > 1:
+        inp["e"] = inp["e"][:1].expand(batch, -1, -1).contiguous()  # CFG: shared timestep
+    freqs = wan_ref.rope_freqs(1024, 128).to(DEV)
+    want32 = run(ref, inp, freqs)
+    want16 = run(stock, inp, freqs)
+    e = inp["e"][:1] if batch > 1 else inp["e"]
+    got = run(fused, inp, freqs, e=e, ctx_dtype=torch.bfloat16)
+    assert rel_l2(got, want32) <= 1e-2 and max_abs(got, want32) <= 5e-2
+    assert rel_l2(got, want16) <= 1e-2 and max_abs(got, want16) <= 5e-2
+
+
+def test_block_per_batch_modulation(pkg):
+    ref, _, fused = make_pair(pkg, seed=8)
+    inp = wan_ref.block_inputs(wan_ref.WAN_1_3B, (1, 10, 20), 2, seed=12, device=DEV)
+    freqs = wan_ref.rope_freqs(1024, 128).to(DEV)
+    want = run(ref, inp, freqs)
+    got = run(fused, inp, freqs, ctx_dtype=torch.bfloat16)  # e differs per batch entry
+    assert rel_l2(got, want) <= 1e-2 and max_abs(got, want) <= 5e-2
+
+
+def test_block_bf16_input_and_carry_chain(pkg):
+    """Layer-0 style bf16 input, then a second block fed through the carried statistics."""
+    ref1, _, f1 = make_pair(pkg, seed=21)
+    ref2, _, f2 = make_pair(pkg, seed=22)
+    inp = wan_ref.block_inputs(wan_ref.WAN_1_3B, (1, 16, 16), 1, seed=13, device=DEV, x_dtype=torch.bfloat16)
+    freqs = wan_ref.rope_freqs(1024, 128).to(DEV)
+    with torch.no_grad():
+        w = run(ref1, inp, freqs)
+        w = run(ref2, inp, freqs, x=w)
+        g = run(f1, inp, freqs, ctx_dtype=torch.bfloat16)
+        g = run(f2, inp, freqs, x=g, ctx_dtype=torch.bfloat16)
+    assert rel_l2(g, w) <= 1e-2 and max_abs(g, w) <= 5e-2
+
+
+def test_block_production_shape_cfg1(pkg):
+    """Config 1: one block, grid (21, 30, 52) = 32760 tokens, bf16, vs the fp32 oracle."""
+    ref, _, fused = make_pair(pkg, seed=9, jitter=0.0)
+    inp = wan_ref.block_inputs(wan_ref.WAN_1_3B, (21, 30, 52), 1, seed=14, device=DEV)
+    freqs = wan_ref.rope_freqs(1024, 128).to(DEV)
+    want = run(ref, inp, freqs)
+    got = run(fused, inp, freqs, ctx_dtype=torch.bfloat16)
+    assert rel_l2(got, want) <= 1e-2 and max_abs(got, want) <= 5e-2
+
+
+def test_alias_audit(pkg):
+    _, _, fused = make_pair(pkg)
+    audit = fused.alias_audit()
+    assert audit["all_share_storage"], audit
+
+
+def test_model_forward_matches_oracle(pkg):
+    """Three-layer DiT (CFG batch 2, shared timestep) vs the oracle model in fp32."""
+    cfg = wan_ref.WAN_1_3B
+    ref = wan_ref.init_weights_(wan_ref.WanModelRef(cfg, torch.float32, num_layers=3), seed=31).to(DEV)
+    params = pkg.build_wan(pkg.WAN_1_3B, seed=0, device=DEV, num_layers=3)
+    params.load_state_dict(ref.state_dict(), strict=True)
+    params.to(torch.bfloat16)
+    params.time_embedding.float()
+    params.time_projection.float()
+    for b in params.blocks:
+        b.modulation.data = b.modulation.data.float()
+    params.head.modulation.data = params.head.modulation.data.float()
+    fused = pkg.FusedWanModel(params)
+    inp = wan_ref.model_inputs(cfg, (2, 16, 24), 2, seed=32, device=DEV)
+    with torch.no_grad():
+        want = ref(inp["x"], inp["t"], inp["context"], inp["seq_len"])
+        got = fused(inp["x"], inp["t"], inp["context"], inp["seq_len"])
+    for g, w in zip(got, want):
+        assert g.shape == w.shape
+        assert rel_l2(g, w) <= 2e-2

@@ -1,0 +1,65 @@
+"""The C ABI library builds, loads and exports every symbol include/wdit.h declares; host-side
+argument validation rejects bad calls before touching a device. CPU only (no compute)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "wdit.h"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(wdit_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib(pkg):
+    return pkg._lib.load(build_if_missing=True)
+
+
+def test_header_declares_the_entry_points():
+    syms = declared_symbols()
+    for s in ("wdit_gemm_act", "wdit_gemm_residual", "wdit_gemm_norm", "wdit_ln_stats", "wdit_fold_weight",
+              "wdit_layernorm_modulation", "wdit_rmsnorm", "wdit_qk_rms_rope_from_partials", "wdit_rope_table"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(lib, pkg):
+    for s in declared_symbols():
+        assert hasattr(lib, s), f"{s} declared in include/wdit.h but not exported"
+    # ...and the Python binding declares a signature for each of them.
+    assert set(declared_symbols()) <= set(pkg._lib.exported_symbols())
+
+
+def test_library_is_built_for_sm100a():
+    so = (ROOT / "coda-wan-dit_b200" / "libwdit.so").read_bytes()
+    assert b"sm_100a" in so or b"sm_100" in so
+
+
+def test_argument_validation_without_device(lib):
+    null = ctypes.c_void_p(None)
+    # NULL operands -> WDIT_ERR_ARG; bad shapes -> WDIT_ERR_SHAPE; no CUDA call is reached.
+    assert lib.wdit_gemm_act(null, 64, null, 64, null, 64, 128, 256, 64, null, 0, null, null, 0, 0, 0.0, null, 0) == 1
+    dummy = ctypes.c_void_p(0x1000)
+    assert lib.wdit_gemm_act(dummy, 64, dummy, 64, dummy, 64, 128, 100, 64, null, 0, null, null, 0, 0, 0.0, null,
+                             0) == 2  # N % 64 != 0
+    assert lib.wdit_gemm_act(dummy, 32, dummy, 64, dummy, 256, 128, 256, 64, null, 0, null, null, 0, 0, 0.0, null,
+                             0) == 2  # lda < K
+    assert lib.wdit_gemm_residual(dummy, 64, dummy, 64, null, 256, dummy, 256, 128, 256, 64, null, null, null, 0, 0,
+                                  null, 0, null, null, 0) == 1  # no residual
+    assert lib.wdit_ln_stats(null, 0, 64, 4, 64, null, null, null, null) == 1
+    assert lib.wdit_fold_weight(dummy, 60, 4, 60, 1.0, null, null, null, null, null, dummy, 60, dummy, dummy,
+                                null) == 2  # K % 8 != 0
+
+
+def test_norm_workspace_size(lib):
+    # partials: M x (groups * width/256) fp32, counters: m_blocks x groups u32, each 256-B rounded
+    M, groups, width = 1000, 2, 1536
+    part = ((M * groups * (width // 256) * 4 + 255) // 256) * 256
+    ctr = (((M + 127) // 128 * groups * 4 + 255) // 256) * 256
+    assert lib.wdit_gemm_norm_workspace_bytes(M, 4608, groups, width) == part + ctr
+    assert lib.wdit_stats_tile_width() == 256

@@ -1,0 +1,70 @@
+"""Token-sharded self-attention regrouping on CPU ranks (gloo, world size 2 and 4): the layout
+maps of oracle/ulysses_ref.py around a real all_to_all reproduce full-sequence attention.
+Also: the unit assignment covers every (batch, head) pair once, including 12 heads x CFG
+batch 2 on 8 ranks."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+from oracle import ulysses_ref
+
+
+@pytest.mark.parametrize("B,H,P", [(2, 12, 8), (1, 12, 4), (2, 12, 2), (2, 40, 8), (1, 40, 8)])
+def test_unit_assignment_is_a_partition(B, H, P):
+    U, owner = ulysses_ref.units(B, H, P)
+    flat = [bh for d in owner for bh in d]
+    assert len(flat) == B * H == len(set(flat)) and U * P == B * H
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, B, L, H, hd, q, k, v, ret):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        Lp = L // world
+        D = H * hd
+        rows = torch.cat([t[:, rank * Lp:(rank + 1) * Lp].reshape(B * Lp, D) for t in (q, k, v)], dim=1)
+        U = B * H // world
+        send = ulysses_ref.pack(rows, B, Lp, H, hd, 3, world)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send)
+        full = ulysses_ref.seq_gather(recv, 3, U, world, Lp, hd)
+        o = F.scaled_dot_product_attention(full[0][None], full[1][None], full[2][None])[0]
+        send2 = ulysses_ref.seq_scatter(o, U, world, Lp, hd)
+        recv2 = torch.empty_like(send2)
+        dist.all_to_all_single(recv2, send2)
+        y = ulysses_ref.unpack(recv2, B, Lp, H, hd, world)
+        ret[rank] = y
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,B,H", [(2, 2, 12), (4, 2, 12)])
+def test_regroup_equals_full_attention(world, B, H):
+    torch.manual_seed(0)
+    L, hd = 8 * world, 16
+    q, k, v = (torch.randn(B, L, H * hd) for _ in range(3))
+    mgr = mp.Manager()
+    ret = mgr.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), B, L, H, hd, q, k, v, ret), nprocs=world,
+                       start_method="spawn", join=True)
+    Lp = L // world
+    ref = F.scaled_dot_product_attention(
+        q.view(B, L, H, hd).transpose(1, 2), k.view(B, L, H, hd).transpose(1, 2), v.view(B, L, H, hd).transpose(1, 2)
+    ).transpose(1, 2).reshape(B, L, H * hd)
+    for r in range(world):
+        want = ref[:, r * Lp:(r + 1) * Lp].reshape(B * Lp, H * hd)
+        assert torch.allclose(ret[r], want, atol=1e-5, rtol=1e-5)

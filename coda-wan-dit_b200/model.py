@@ -208,6 +208,14 @@ class FusedWanModel(nn.Module):
         self.b_head = model.head.head.bias.detach().float()
         self.head_mod = model.head.modulation.detach().float().reshape(2, self.dim).contiguous()
         self.eps = float(getattr(model.head.norm, "eps", 1e-6))
+        # Module.to(dtype) casts a complex buffer to a real dtype (dropping the imaginary part),
+        # so keep an own complex128 copy of the rotary frequencies.
+        fr = getattr(model, "freqs", None)
+        head_dim = self.dim // int(model.num_heads)
+        if fr is None or not fr.is_complex():
+            fr = rope_freqs(1024, head_dim)
+        self.register_buffer("freqs", fr.to(device=model.patch_embedding.weight.device, dtype=torch.complex128),
+                             persistent=False)
 
     # -- embeddings --------------------------------------------------------
     def embed_tokens(self, x_list, seq_len):
@@ -285,7 +293,7 @@ class FusedWanModel(nn.Module):
             seq_lens_arg = None
         x = x.contiguous()
         for blk in self.model.blocks:
-            x = blk(x, e0, seq_lens_arg, grid_sizes, self.model.freqs, context, None)
+            x = blk(x, e0, seq_lens_arg, grid_sizes, self.freqs, context, None)
         x32 = x.reshape(B * Lx, self.dim)
         carried = self.carry.get(x32)
         y = self.head(x32, e, carried, B * Lx, shared_e)

@@ -123,10 +123,11 @@ def gemm_residual(a, w, c, *, out=None, bias=None, gate_a=None, gate_b=None, gat
     if out is None:
         out = torch.empty_like(c)
     assert out.dtype == torch.float32 and out.shape == (M, N) and out.stride(1) == 1
+    bias = _f32vec(bias)  # keep converted operands referenced until the launch is enqueued
     call(
         "wdit_gemm_residual",
         ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(c), c.stride(0), ptr(out), out.stride(0), M, N, K,
-        ptr(_f32vec(bias)), ptr(gate_a), ptr(gate_b), gate_b_stride, rows_per_batch,
+        ptr(bias), ptr(gate_a), ptr(gate_b), gate_b_stride, rows_per_batch,
         ptr(x_bf16_out), 0 if x_bf16_out is None else x_bf16_out.stride(0), ptr(stats_out),
         stream_ptr(), max_ctas,
     )
@@ -184,10 +185,11 @@ def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_w
         nbytes = ws.numel()
     w0 = _f32vec(norm_w[0]) if norm_groups > 0 else None
     w1 = _f32vec(norm_w[1]) if norm_groups > 1 else None
+    vec = _f32vec(vec)
     call(
         "wdit_gemm_norm",
         ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(out), out.stride(0), M, N, K,
-        ptr(_f32vec(vec)), *_ln_args(ln, K), norm_groups, norm_width, ptr(w0), ptr(w1), float(norm_eps),
+        ptr(vec), *_ln_args(ln, K), norm_groups, norm_width, ptr(w0), ptr(w1), float(norm_eps),
         rope_groups, ptr(rope_cos), ptr(rope_sin), rows_per_batch, token_offset, ptr(ws), nbytes,
         stream_ptr(), max_ctas,
     )
@@ -222,10 +224,11 @@ def fold_weight(w, *, mult_c, mult_a=None, mult_b=None, shift_a=None, shift_b=No
         csum_out = torch.empty(N, dtype=torch.float32, device=w.device)
     if vec_out is None:
         vec_out = torch.empty(N, dtype=torch.float32, device=w.device)
+    bias = _f32vec(bias)
     call(
         "wdit_fold_weight",
         ptr(w), w.stride(0), N, K, float(mult_c), ptr(mult_a), ptr(mult_b), ptr(shift_a), ptr(shift_b),
-        ptr(_f32vec(bias)), ptr(w_out), w_out.stride(0), ptr(csum_out), ptr(vec_out), stream_ptr(),
+        ptr(bias), ptr(w_out), w_out.stride(0), ptr(csum_out), ptr(vec_out), stream_ptr(),
     )
     return w_out, csum_out, vec_out
 
@@ -242,10 +245,11 @@ def layernorm_modulation_bf16(x: torch.Tensor, scale: torch.Tensor, shift: torch
     _require_cuda(x2)
     x2 = _rowmajor(x2)
     out = torch.empty((x2.shape[0], DIM), dtype=torch.bfloat16, device=x.device)
+    scale, shift = _f32vec(scale), _f32vec(shift)
     call(
         "wdit_layernorm_modulation",
         ptr(x2), 1 if x2.dtype == torch.bfloat16 else 0, x2.stride(0), x2.shape[0], DIM,
-        ptr(_f32vec(scale)), ptr(_f32vec(shift)), float(eps), ptr(out), DIM, stream_ptr(),
+        ptr(scale), ptr(shift), float(eps), ptr(out), DIM, stream_ptr(),
     )
     return out.view(shape)
 
@@ -280,10 +284,12 @@ def qk_rms_rope_from_partials(qk, partial, q_weight, k_weight, cos, sin, eps):
     assert cos.shape == sin.shape == (m, HEAD_DIM // 2)
     _require_cuda(qk, partial, cos, sin)
     assert qk.stride(1) == 1 and partial.is_contiguous()
+    wq, wk = _f32vec(q_weight), _f32vec(k_weight)
+    cos, sin = cos.float().contiguous(), sin.float().contiguous()
     call(
         "wdit_qk_rms_rope_from_partials",
-        ptr(qk), qk.stride(0), ptr(partial), m, DIM, ptr(_f32vec(q_weight)), ptr(_f32vec(k_weight)),
-        ptr(cos.float().contiguous()), ptr(sin.float().contiguous()), float(eps), stream_ptr(),
+        ptr(qk), qk.stride(0), ptr(partial), m, DIM, ptr(wq), ptr(wk),
+        ptr(cos), ptr(sin), float(eps), stream_ptr(),
     )
     return qk[:, :DIM], qk[:, DIM:]
 
@@ -313,7 +319,8 @@ def rmsnorm_fused(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Te
     _require_cuda(x2)
     x2 = _rowmajor(x2.to(torch.bfloat16) if x2.dtype != torch.bfloat16 else x2)
     out = torch.empty((x2.shape[0], DIM), dtype=torch.bfloat16, device=x.device)
-    call("wdit_rmsnorm", ptr(x2), x2.stride(0), x2.shape[0], DIM, ptr(_f32vec(weight)), float(eps), ptr(out), DIM,
+    weight = _f32vec(weight)
+    call("wdit_rmsnorm", ptr(x2), x2.stride(0), x2.shape[0], DIM, ptr(weight), float(eps), ptr(out), DIM,
          stream_ptr())
     return out.view(shape)
 

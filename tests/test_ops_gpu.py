@@ -166,26 +166,47 @@ def test_reference_api_layernorm_modulation_golden(pkg):
     s, sh = torch.from_numpy(z["scale"]).to(DEV), torch.from_numpy(z["shift"]).to(DEV)
     got = pkg.ops.layernorm_modulation_bf16(x, s, sh, float(z["eps"])).cpu()
     want_rz = bf16(z["out"])
-    d = (got.view(torch.int16).int() - want_rz.view(torch.int16).int()).abs()
+    d = ulps(got, want_rz)
     assert int(d.max()) <= 1  # RNE on the GPU vs round-toward-zero in the fixture
     ref_rne = fused_ref.layernorm_modulation(torch.from_numpy(z["x"]), torch.from_numpy(z["scale"]),
                                              torch.from_numpy(z["shift"]), float(z["eps"]))
     assert (got.view(torch.int16) == ref_rne.view(torch.int16)).float().mean().item() > 0.99
 
 
+def _ordered(t):
+    x = t.cpu().contiguous().view(torch.int16).int()
+    return torch.where(x < 0, -(x & 0x7FFF), x)  # sign-magnitude bf16 bits -> monotone integers
+
+
+def ulps(a, b):
+    """Distance in bf16 units in the last place (across zero too)."""
+    return (_ordered(a) - _ordered(b)).abs()
+
+
 def test_reference_api_rmsnorm_and_qk_rope_golden(pkg):
+    # The fixtures were rounded toward zero (Triton CPU interpreter) at every bf16 step; the
+    # GPU rounds to nearest even. The oracle reproduces the fixtures bit-exactly in "rz" mode
+    # (CPU tests); here the GPU output must match the same oracle in "rne" mode on the fixture
+    # inputs, and stay within a few ulps of the fixture itself.
     z = np.load(GOLD / "rmsnorm.npz")
-    got = pkg.ops.rmsnorm_fused(bf16(z["x"]).to(DEV), bf16(z["w"]).to(DEV), float(z["eps"])).cpu()
-    d = (got.view(torch.int16).int() - bf16(z["out"]).view(torch.int16).int()).abs()
-    assert int(d.max()) <= 1
+    x, w = bf16(z["x"]), bf16(z["w"])
+    got = pkg.ops.rmsnorm_fused(x.to(DEV), w.to(DEV), float(z["eps"])).cpu()
+    d = ulps(got, fused_ref.rmsnorm(x, w, float(z["eps"])))
+    assert int(d.max()) <= 1 and (d == 0).float().mean().item() > 0.99
+    assert torch.allclose(got.float(), bf16(z["out"]).float(), rtol=2.0**-6, atol=2e-2)
     z = np.load(GOLD / "qk_rms_rope.npz")
-    qk = bf16(z["qk"]).to(DEV)
-    q, k = pkg.ops.qk_rms_rope_from_partials(qk, torch.from_numpy(z["partial"]).to(DEV), bf16(z["wq"]).to(DEV),
-                                             bf16(z["wk"]).to(DEV), torch.from_numpy(z["cos"]).to(DEV),
-                                             torch.from_numpy(z["sin"]).to(DEV), float(z["eps"]))
-    for got, key in ((q, "q"), (k, "k")):
-        d = (got.cpu().contiguous().view(torch.int16).int() - bf16(z[key]).view(torch.int16).int()).abs()
-        assert int(d.max()) <= 2
+    qk = bf16(z["qk"])
+    args = (torch.from_numpy(z["partial"]), bf16(z["wq"]), bf16(z["wk"]), torch.from_numpy(z["cos"]),
+            torch.from_numpy(z["sin"]), float(z["eps"]))
+    q, k = pkg.ops.qk_rms_rope_from_partials(qk.clone().to(DEV), *[a.to(DEV) if torch.is_tensor(a) else a
+                                                                    for a in args])
+    qr, kr = fused_ref.qk_rms_rope_from_partials(qk.clone(), *args)
+    for got, ref, key in ((q, qr, "q"), (k, kr, "k")):
+        d = ulps(got, ref)
+        assert int(d.max()) <= 1 and (d == 0).float().mean().item() > 0.99
+        # vs the fixture itself: ~4 bf16 ulps at unit scale (rotations that cancel to ~0 can land
+        # on either side of zero under the two rounding modes, so no ulp bound there)
+        assert torch.allclose(got.cpu().float(), bf16(z[key]).float(), rtol=2.0**-6, atol=2e-2)
 
 
 def test_reference_api_rope_table_golden(pkg):

@@ -20,9 +20,11 @@ def bf16(a: np.ndarray) -> torch.Tensor:
 def ulp_close(got: torch.Tensor, want: torch.Tensor, max_ulps: int = 1, min_exact: float = 0.99):
     """bf16 tensors equal up to `max_ulps` units in the last place, mostly bit-exact
     (reduction order may move a rounding boundary)."""
-    g = got.contiguous().view(torch.int16).to(torch.int32)
-    w = want.contiguous().view(torch.int16).to(torch.int32)
-    d = (g - w).abs()
+    def ordered(t):  # sign-magnitude bf16 bits -> monotone integers
+        x = t.contiguous().view(torch.int16).to(torch.int32)
+        return torch.where(x < 0, -(x & 0x7FFF), x)
+
+    d = (ordered(got) - ordered(want)).abs()
     assert int(d.max()) <= max_ulps, f"max ulp diff {int(d.max())}"
     assert float((d == 0).float().mean()) >= min_exact
 

@@ -27,6 +27,7 @@ WDIT_ERR_NAMES = {
     5: "workspace missing or too small",
     6: "tensor map rejected by the driver",
     7: "driver entry point unavailable",
+    8: "problem exceeds the static scratch limit",
 }
 
 P = c_void_p
@@ -47,6 +48,11 @@ _SIGNATURES = {
         c_int,
         [P, I, P, I, P, I, I, I, I, P, P, P, I, I, F, I, I, P, P, F, I, P, P, I, I, P, c_longlong, P, I],
     ),
+    "wdit_gemm_norm_static": (
+        c_int,
+        [P, I, P, I, P, I, I, I, I, P, P, P, I, I, F, I, I, P, P, F, I, P, P, I, I, P, I],
+    ),
+    "wdit_static_scratch_bytes": (c_longlong, []),
     "wdit_ln_stats": (c_int, [P, I, I, I, I, P, P, P, P]),
     "wdit_fold_weight": (c_int, [P, I, I, I, F, P, P, P, P, P, P, I, P, P, P]),
     "wdit_layernorm_modulation": (c_int, [P, I, I, I, I, P, P, F, P, I, P]),
@@ -122,7 +128,7 @@ def call(name: str, *args) -> int:
     if name in _LAUNCHING:
         launch_counter["n"] += 1
     rc = getattr(lib, name)(*args)
-    if name.startswith("wdit_") and isinstance(rc, int) and name not in ("wdit_gemm_norm_workspace_bytes",):
+    if isinstance(rc, int) and name not in ("wdit_gemm_norm_workspace_bytes", "wdit_static_scratch_bytes"):
         check(rc, name)
     return rc
 

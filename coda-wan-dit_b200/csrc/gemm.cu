@@ -945,3 +945,116 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of wdit_gemm_norm.
+//
+// Some callers cannot allocate device memory at the point where they run this GEMM: code
+// that executes inside a region where allocation is not permitted (for example while
+// another component is recording work for replay, or inside a fixed memory budget that
+// was reserved up front), and hosts whose allocator is owned by a different runtime and
+// is not reachable from the call site. For them the row-statistics scratch lives in a
+// fixed, file-scope device array instead of a caller-supplied workspace.
+//
+// Limits and sharing rules:
+//   * The array holds WDIT_STATIC_SCRATCH_BYTES (4 MiB) on every GPU that loads this
+//     library, for the lifetime of the process.
+//   * A call needs wdit_gemm_norm_workspace_bytes(M, N, norm_groups, norm_width) bytes of
+//     it; larger problems are rejected with WDIT_ERR_SCRATCH_LIMIT before any launch.
+//   * All calls on a device share the one array and it keeps the last call's contents.
+//     The arrival counters must start at zero, so each call clears them (cudaMemsetAsync
+//     on the caller's stream) before its launch; calls that overlap on the GPU (different
+//     streams with no ordering between them) race on the array.
+//   * The first call on a device looks the array's device address up once
+//     (cudaGetSymbolAddress, with that device current); make that first call before any
+//     stream capture begins.
+// ---------------------------------------------------------------------------
+namespace wdit {
+namespace {
+
+static __device__ __align__(256) unsigned char g_norm_static_scratch[WDIT_STATIC_SCRATCH_BYTES];
+
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch_addr[64] = {};
+
+// Device address of the static scratch on the current device (looked up once per device).
+int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+  if (dev < 0 || dev >= 64) return WDIT_ERR_ARG;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_addr[dev] == nullptr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_norm_static_scratch);
+    if (e != cudaSuccess || addr == nullptr) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+    g_static_scratch_addr[dev] = addr;
+  }
+  *out = g_static_scratch_addr[dev];
+  return WDIT_OK;
+}
+
+}  // namespace
+}  // namespace wdit
+
+extern "C" {
+
+long long wdit_static_scratch_bytes(void) { return WDIT_STATIC_SCRATCH_BYTES; }
+
+int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                          const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                          int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
+                          const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
+                          const float* rope_sin, int rows_per_batch, int token_offset, void* stream, int max_ctas) {
+  int rc = check_common(A, lda, B, ldb, M, N, K);
+  if (rc) return rc;
+  if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
+  if (norm_groups < 1 || norm_groups > 2 || rope_groups < 0 || rope_groups > norm_groups) return WDIT_ERR_ARG;
+  if (norm_width <= 0 || norm_width % BN != 0 || norm_groups * norm_width > N) return WDIT_ERR_SHAPE;
+  if (norm_w0 == nullptr || (norm_groups > 1 && norm_w1 == nullptr)) return WDIT_ERR_ARG;
+  if (!aligned16(norm_w0) || (norm_w1 && !aligned16(norm_w1))) return WDIT_ERR_ALIGN;
+  if (rope_groups > 0) {
+    if (rope_cos == nullptr || rope_sin == nullptr || rows_per_batch <= 0 || token_offset < 0) return WDIT_ERR_ARG;
+    if (!aligned16(rope_cos) || !aligned16(rope_sin)) return WDIT_ERR_ALIGN;
+    if (norm_width % 128 != 0) return WDIT_ERR_SHAPE;
+  }
+  if (vec != nullptr && !aligned16(vec)) return WDIT_ERR_ALIGN;
+  const long long need = wdit_gemm_norm_workspace_bytes(M, N, norm_groups, norm_width);
+  if (need > static_cast<long long>(WDIT_STATIC_SCRATCH_BYTES)) return WDIT_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if ((rc = static_scratch_address(&scratch))) return rc;
+
+  EpiParams p = {};
+  rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
+  if (rc) return rc;
+  p.vec = vec;
+  p.norm_groups = norm_groups;
+  p.norm_width = norm_width;
+  p.norm_w[0] = norm_w0;
+  p.norm_w[1] = norm_w1;
+  p.norm_eps = norm_eps;
+  p.rope_groups = rope_groups;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
+  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
+  p.token_offset = token_offset;
+  p.has_out_map = 1;
+  const long long part_cols = static_cast<long long>(norm_groups) * (norm_width / BN);
+  const long long part_bytes = ((static_cast<long long>(M) * part_cols * 4 + 255) / 256) * 256;
+  const long long ctr_bytes = need - part_bytes;
+  p.part = reinterpret_cast<float*>(scratch);
+  p.counters = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(scratch) + part_bytes);
+  // The counters start every launch at zero (the array keeps whatever the last call left).
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, static_cast<size_t>(ctr_bytes), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+
+  CUtensorMap ma, mb, mo, none;
+  memset(&none, 0, sizeof(none));
+  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  return launch<kEpiNorm>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), true,
+                          max_ctas, norm_width / BN);
+}
+
+}  // extern "C"

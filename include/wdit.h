@@ -33,6 +33,10 @@ extern "C" {
 #define WDIT_ERR_WORKSPACE 5  /* workspace missing or too small */
 #define WDIT_ERR_TMAP 6       /* cuTensorMapEncodeTiled rejected a descriptor */
 #define WDIT_ERR_DRIVER 7     /* driver entry point unavailable */
+#define WDIT_ERR_SCRATCH_LIMIT 8 /* problem needs more than the static scratch of wdit_gemm_norm_static */
+
+/* Size of the fixed device scratch array used by wdit_gemm_norm_static (per GPU). */
+#define WDIT_STATIC_SCRATCH_BYTES (4ll << 20)
 #define WDIT_ERR_CUDA_BASE 1000
 
 /* ---- runtime / diagnostics (no reference counterpart; the reference uses Python asserts) ---- */
@@ -101,6 +105,28 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
                    const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos, const float* rope_sin,
                    int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes, void* stream,
                    int max_ctas);
+
+/*
+ * wdit_gemm_norm without a workspace argument: it allocates nothing and takes no scratch from
+ * the caller. No counterpart in the reference (which always allocates through PyTorch); it is
+ * for callers that cannot allocate device memory where they issue this GEMM, e.g. code running
+ * where allocation is not allowed or with an allocator owned by another runtime.
+ * Same arguments and result as wdit_gemm_norm (norm_groups >= 1). The row-statistics scratch
+ * is a fixed array of WDIT_STATIC_SCRATCH_BYTES (4 MiB) per GPU, held for the life of the
+ * process; problems needing more (wdit_gemm_norm_workspace_bytes > 4 MiB, e.g. QKV beyond
+ * ~87k rows) return WDIT_ERR_SCRATCH_LIMIT. Every call on a device shares that array: calls
+ * that overlap on the GPU race. Each call zeroes the array's counters on `stream` first. The
+ * first call on a device looks the array's address up (with this library's current device,
+ * see wdit_set_device); make it before any stream capture.
+ */
+int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                          const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                          int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
+                          const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
+                          const float* rope_sin, int rows_per_batch, int token_offset, void* stream, int max_ctas);
+
+/* Bytes of the static scratch array of wdit_gemm_norm_static (= WDIT_STATIC_SCRATCH_BYTES). */
+long long wdit_static_scratch_bytes(void);
 
 /* ---- memory-bound passes ---- */
 

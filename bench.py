@@ -247,14 +247,16 @@ def run_ours(args) -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    def timed(fn, k):
+    def timed(fn, k, tag):
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push(tag)
         e0.record()
         for _ in range(k):
             fn()
         e1.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         ms = torch.tensor([e0.elapsed_time(e1) / k], device=dev)
         if world > 1:
@@ -276,7 +278,7 @@ def run_ours(args) -> None:
         clocks = ClockSampler(local)
         clocks.start()
         n0 = pkg._lib.launch_counter["n"]
-        ms = timed(forward_resident, args.steps)
+        ms = timed(forward_resident, args.steps, "timed_resident")
         launches = pkg._lib.launch_counter["n"] - n0
         clk = clocks.stop()
         for blk in model.model.blocks:
@@ -284,7 +286,7 @@ def run_ours(args) -> None:
         k_ms = [a.elapsed_time(b) for a, b, _ in timer]
         k_flops = timer[0][2] if timer else 0.0
         # Timed region 2: end to end from host buffers.
-        ms_e2e = timed(forward_e2e, args.steps)
+        ms_e2e = timed(forward_e2e, args.steps, "timed_e2e")
         pkg._lib.raise_on_device_error()
 
     peaks = load_peaks()

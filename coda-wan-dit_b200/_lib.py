@@ -46,11 +46,11 @@ _SIGNATURES = {
     "wdit_gemm_norm_workspace_bytes": (c_longlong, [I, I, I, I]),
     "wdit_gemm_norm": (
         c_int,
-        [P, I, P, I, P, I, I, I, I, P, P, P, I, I, F, I, I, P, P, F, I, P, P, I, I, P, c_longlong, P, I],
+        [P, I, P, I, P, I, I, I, I, P, P, P, I, I, F, I, I, P, P, F, I, P, P, I, I, I, P, c_longlong, P, I],
     ),
     "wdit_gemm_norm_static": (
         c_int,
-        [P, I, P, I, P, I, I, I, I, P, P, P, I, I, F, I, I, P, P, F, I, P, P, I, I, P, I],
+        [P, I, P, I, P, I, I, I, I, P, P, P, I, I, F, I, I, P, P, F, I, P, P, I, I, I, P, I],
     ),
     "wdit_static_scratch_bytes": (c_longlong, []),
     "wdit_ln_stats": (c_int, [P, I, I, I, I, P, P, P, P]),
@@ -58,7 +58,7 @@ _SIGNATURES = {
     "wdit_layernorm_modulation": (c_int, [P, I, I, I, I, P, P, F, P, I, P]),
     "wdit_rmsnorm": (c_int, [P, I, I, I, P, F, P, I, P]),
     "wdit_qk_rms_rope_from_partials": (c_int, [P, I, P, I, I, P, P, P, P, F, P]),
-    "wdit_rope_table": (c_int, [P, I, I, I, I, P, P, P]),
+    "wdit_rope_table": (c_int, [P, I, I, I, I, I, P, P, P]),
     "wdit_block_mean_sq": (c_int, [P, I, I, I, I, P, P]),
     "wdit_ulysses_pack": (c_int, [P, I, I, I, I, I, I, I, P, P]),
     "wdit_seq_gather": (c_int, [P, I, I, I, I, I, P, P]),

@@ -181,7 +181,8 @@ class FusedWanBlock(nn.Module):
                              persistent=False)
         self._rope = {}
         if rope_cos is not None and rope_sin is not None:
-            self._rope["given"] = (rope_cos.float().contiguous(), rope_sin.float().contiguous())
+            # reference layout [tokens, 64] -> pair-major [64, tokens]
+            self._rope["given"] = (rope_cos.float().t().contiguous(), rope_sin.float().t().contiguous())
 
     # ------------------------------------------------------------------
     def _rope_tables(self, grid, freqs):
@@ -190,7 +191,7 @@ class FusedWanBlock(nn.Module):
         key = (tuple(grid), freqs.data_ptr())
         tab = self._rope.get(key)
         if tab is None:
-            tab = ops.build_wan_rope_table(grid, freqs)
+            tab = ops.build_rope_table_pair_major(grid, freqs)
             self._rope = {key: tab}
         return tab
 

@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(256)
 
 // ---------------------------------------------------------------------------
 __global__ void rope_table_kernel(const double* __restrict__ freqs_ri, int max_pos, int f, int h, int w,
-                                  float* __restrict__ cos_out, float* __restrict__ sin_out) {
+                                  int pair_major, float* __restrict__ cos_out, float* __restrict__ sin_out) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(f) * h * w * 64;
   if (idx >= total) return;
@@ -258,8 +258,9 @@ __global__ void rope_table_kernel(const double* __restrict__ freqs_ri, int max_p
   const int pos = pair < 22 ? fi : (pair < 43 ? hi : wi);
   const double re = freqs_ri[(static_cast<size_t>(pos) * 64 + pair) * 2];
   const double im = freqs_ri[(static_cast<size_t>(pos) * 64 + pair) * 2 + 1];
-  cos_out[idx] = static_cast<float>(re);
-  sin_out[idx] = static_cast<float>(im);
+  const long long o = pair_major ? static_cast<long long>(pair) * (total >> 6) + tok : idx;
+  cos_out[o] = static_cast<float>(re);
+  sin_out[o] = static_cast<float>(im);
 }
 
 inline int launch_status() {
@@ -334,14 +335,14 @@ int wdit_qk_rms_rope_from_partials(void* qk, int ldqk, const float* partial, int
   return launch_status();
 }
 
-int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, float* cos_out, float* sin_out,
-                    void* stream) {
+int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, int pair_major, float* cos_out,
+                    float* sin_out, void* stream) {
   if (freqs_ri == nullptr || cos_out == nullptr || sin_out == nullptr) return WDIT_ERR_ARG;
   if (f <= 0 || h <= 0 || w <= 0 || f > max_pos || h > max_pos || w > max_pos) return WDIT_ERR_SHAPE;
   const long long total = static_cast<long long>(f) * h * w * 64;
   const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
-  rope_table_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(freqs_ri, max_pos, f, h, w, cos_out,
-                                                                            sin_out);
+  rope_table_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(freqs_ri, max_pos, f, h, w, pair_major,
+                                                                            cos_out, sin_out);
   return launch_status();
 }
 

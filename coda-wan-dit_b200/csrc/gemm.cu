@@ -53,12 +53,17 @@ namespace wdit {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
-constexpr int kEpiThreads = 128;
+constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiThreads = 128;  // one column half (4 warps)
+constexpr uint32_t kStgBytes = 8192;  // 128 rows x 32 bf16 output staging tile
 constexpr uint32_t kTileABytes = BM * BK * 2;  // 16 KB
 constexpr uint32_t kTileBBytes = BN * BK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kTmemCols = 2 * BN;  // two accumulator buffers
+// Norm-GEMM workspace layout: a fixed region of arrival counters first, then the per-row
+// partials. The counters sit at the same place for every problem shape, so launches of
+// different shapes can share one workspace (partials never overwrite counters).
+constexpr long long kCounterRegionBytes = 64 * 1024;
 
 enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiNorm = 2 };
 
@@ -67,20 +72,24 @@ struct Cfg;
 template <>
 struct Cfg<kEpiAct> {
   static constexpr int kStages = 4;
-  static constexpr uint32_t kEpiBytes = 2 * 16384;  // 2 x (128 rows x 64 bf16), 128B swizzle
+  // 2 halves x 2 staging tiles (128 rows x 32 bf16, 64-byte swizzle) + 128 floats
+  static constexpr uint32_t kEpiBytes = 4 * kStgBytes + 512;
   static constexpr int kNumCBuf = 0;
+  static constexpr int kEpiArrivals = 2 * kEpiThreads;
 };
 template <>
 struct Cfg<kEpiNorm> {
   static constexpr int kStages = 4;
-  static constexpr uint32_t kEpiBytes = 2 * 16384;
+  static constexpr uint32_t kEpiBytes = 4 * kStgBytes + 512;
   static constexpr int kNumCBuf = 0;
+  static constexpr int kEpiArrivals = 2 * kEpiThreads;
 };
 template <>
 struct Cfg<kEpiResidual> {
   static constexpr int kStages = 3;
   static constexpr int kNumCBuf = 4;  // 128 rows x 32 fp32 (16 KB) residual/out ring
   static constexpr uint32_t kEpiBytes = kNumCBuf * 16384 + 2 * 8192;  // + 2 x (128 x 32 bf16)
+  static constexpr int kEpiArrivals = kEpiThreads;
 };
 
 template <int KIND>
@@ -172,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
-      mbar_init(&tempty_bar[i], kEpiThreads);
+      mbar_init(&tempty_bar[i], Cfg<KIND>::kEpiArrivals);
     }
     for (int i = 0; i < 4; ++i) mbar_init(&cload_bar[i], 1);
     fence_mbar_init();
@@ -263,81 +272,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ----------------------------- Epilogue ---------------------------------
-    const int et = threadIdx.x - 64;  // 0..127
-    const int wq = warp & 3;          // TMEM lane quadrant this warp may access
+    // Warps 2..9. Warp w may access TMEM lanes [32*(w%4), 32*(w%4)+32), so its thread owns
+    // accumulator row r = 32*(w%4) + lane. Warps 2..5 take the tile's columns [0, 128),
+    // warps 6..9 columns [128, 256): two warps per scheduler hide each other's latency.
+    // The residual epilogue (bandwidth-bound, shared-memory limited) uses warps 2..5 only.
+    const int ew = warp - 2;          // 0..7
+    const int wq = warp & 3;          // TMEM lane quadrant
+    const int half = ew >> 2;         // column half of the tile
+    const int ht = (ew & 3) * 32 + lane;  // thread index inside its half, 0..127
     const int r = wq * 32 + lane;     // accumulator row inside the tile
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const int col_base = half * (BN / 2);
 
-    if constexpr (KIND == kEpiAct) {
-      const uint32_t stg0 = smem_u32(epi_base);
-      int sbuf = 0;
-      int it = 0;
-      for (int tile = blockIdx.x; tile < s.tiles; tile += gridDim.x, ++it) {
-        const int m_blk = tile / s.n_blocks;
-        const int n_blk = tile - m_blk * s.n_blocks;
-        const int buf = it & 1;
-        const uint32_t tphase = (it >> 1) & 1;
-        {
-          const bool ok = wait_parity(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
-          if (named_bar_any(2, kEpiThreads, !ok)) break;
-        }
-        tc_fence_after();
-        const int row = m_blk * BM + r;
-        float mu = 0.f, rstd = 1.f;
-        const bool use_ln = p.ln.csum != nullptr;
-        if (use_ln && row < s.M) ln_row_stats(p.ln, row, mu, rstd);
-#pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-          const int n0 = n_blk * BN + c * 64;
-          float v[64];
-          const uint32_t ta = tmem_base + lane_off + buf * BN + c * 64;
-          tmem_ld32(ta, &v[0]);
-          tmem_ld32(ta + 32, &v[32]);
-          if (c == BN / 64 - 1) {
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[buf]);
-          }
-          if (n0 >= s.N) continue;  // uniform across the epilogue warps
-          if (use_ln) {
-            float cs[64];
-            load_vec64(p.ln.csum, n0, cs);
-#pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] = rstd * fmaf(-mu, cs[j], v[j]);
-          }
-          if (p.vec != nullptr) {
-            float b[64];
-            load_vec64(p.vec, n0, b);
-#pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] += b[j];
-          }
-          if (p.act == 1) {
-#pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] = gelu_tanh(v[j]);
-          }
-          uint32_t w[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-          const uint32_t stg = stg0 + sbuf * 16384;
-          if (et == 0) bulk_wait_read<1>();
-          named_bar_sync(1, kEpiThreads);
-          stage_row_sw128(stg, r, w);
-          fence_proxy_async_smem();
-          named_bar_sync(1, kEpiThreads);
-          if (et == 0) {
-            tma_store_2d(&tmOut, epi_base + sbuf * 16384, n0, m_blk * BM);
-            bulk_commit();
-          }
-          sbuf ^= 1;
-        }
-      }
-      if (et == 0) bulk_wait_all<0>();
-    } else if constexpr (KIND == kEpiNorm) {
-      const uint32_t stg0 = smem_u32(epi_base);
-      const int tiles_per_group = p.norm_width / BN;
-      const int part_cols = p.norm_groups * tiles_per_group;
+    if constexpr (KIND == kEpiAct || KIND == kEpiNorm) {
+      constexpr int kChunks = (BN / 2) / 32;  // 32-column chunks per half
+      const uint32_t stg_half = smem_u32(epi_base) + half * 2 * kStgBytes;
+      uint8_t* stg_half_ptr = epi_base + half * 2 * kStgBytes;
+      float* ss_smem = reinterpret_cast<float*>(epi_base + 4 * kStgBytes);
+      const uint32_t bar_half = 1 + half;
+      const int tiles_per_group = KIND == kEpiNorm ? p.norm_width / BN : 1;
+      const int part_cols = KIND == kEpiNorm ? p.norm_groups * tiles_per_group : 1;
       int sbuf = 0;
       int it = 0;
       bool failed = false;
+      // Counter of the previous tile's group, released (second-round arrival) only once all
+      // eight warps have passed the next tile-start barrier, i.e. have read its partials.
+      unsigned int* pending_ctr = nullptr;
+      const unsigned int pub_target = 4u * tiles_per_group;  // publishing warps per group
+      auto release_pending = [&]() {
+        if (pending_ctr != nullptr && warp == 2 && lane == 0) {
+          const unsigned int old = atom_add_acq_rel(pending_ctr, 1u);
+          if (old == pub_target + tiles_per_group - 1u) atomicExch(pending_ctr, 0u);
+        }
+        pending_ctr = nullptr;
+      };
       for (int tile = blockIdx.x; tile < s.tiles && !failed; tile += gridDim.x, ++it) {
         const int m_blk = tile / s.n_blocks;
         const int n_blk = tile - m_blk * s.n_blocks;
@@ -345,165 +313,213 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tphase = (it >> 1) & 1;
         {
           const bool ok = wait_parity(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
-          if (named_bar_any(2, kEpiThreads, !ok)) break;
+          if (named_bar_any(3, 2 * kEpiThreads, !ok)) break;
         }
+        if (KIND == kEpiNorm) release_pending();
         tc_fence_after();
         const int row = m_blk * BM + r;
         const bool row_ok = row < s.M;
         float mu = 0.f, rstd = 1.f;
         const bool use_ln = p.ln.csum != nullptr;
         if (use_ln && row_ok) ln_row_stats(p.ln, row, mu, rstd);
-        const int group = (n_blk * BN) / p.norm_width;
-        const bool normed = group < p.norm_groups;
-        const uint32_t tbase = tmem_base + lane_off + buf * BN;
+        const uint32_t tbase = tmem_base + lane_off + buf * BN + col_base;
+        const int group = KIND == kEpiNorm ? (n_blk * BN) / p.norm_width : 0;
+        const bool normed = KIND == kEpiNorm && group < p.norm_groups;
         float rms = 1.f;
+
+        // acc -> LN(acc) + vec for one 32-column chunk starting at column n0.
+        auto finish_linear = [&](float* v, int n0) {
+          if (use_ln) {
+            const float4* cp = reinterpret_cast<const float4*>(p.ln.csum + n0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 c4 = __ldg(cp + q);
+              v[4 * q] = rstd * fmaf(-mu, c4.x, v[4 * q]);
+              v[4 * q + 1] = rstd * fmaf(-mu, c4.y, v[4 * q + 1]);
+              v[4 * q + 2] = rstd * fmaf(-mu, c4.z, v[4 * q + 2]);
+              v[4 * q + 3] = rstd * fmaf(-mu, c4.w, v[4 * q + 3]);
+            }
+          }
+          if (p.vec != nullptr) {
+            const float4* bp = reinterpret_cast<const float4*>(p.vec + n0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 b4 = __ldg(bp + q);
+              v[4 * q] += b4.x;
+              v[4 * q + 1] += b4.y;
+              v[4 * q + 2] += b4.z;
+              v[4 * q + 3] += b4.w;
+            }
+          }
+        };
+
         if (normed) {
-          // Pass 1: this tile's share of the row sum of squares (of the bf16-rounded
-          // projection, as WanRMSNorm sees the bf16 Linear output).
+          // Pass 1 (unrolled): acc -> LN + vec -> bf16 projection, kept packed in registers,
+          // and this thread's share of the row sum of squares (WanRMSNorm normalizes the
+          // bf16 Linear output). The accumulator is released right after, so the MMA of the
+          // next tile overlaps the exchange and pass 2.
+          uint32_t pk[kChunks][16];
           float ss = 0.f;
-#pragma unroll 1
-          for (int c = 0; c < BN / 64; ++c) {
-            const int n0 = n_blk * BN + c * 64;
-            float v[64];
-            tmem_ld32(tbase + c * 64, &v[0]);
-            tmem_ld32(tbase + c * 64 + 32, &v[32]);
-            float b[64];
-            if (use_ln) {
-              load_vec64(p.ln.csum, n0, b);
 #pragma unroll
-              for (int j = 0; j < 64; ++j) v[j] = rstd * fmaf(-mu, b[j], v[j]);
-            }
-            if (p.vec != nullptr) {
-              load_vec64(p.vec, n0, b);
+          for (int c = 0; c < kChunks; ++c) {
+            const int n0 = n_blk * BN + col_base + c * 32;
+            float v[32];
+            tmem_ld32(tbase + c * 32, v);
+            finish_linear(v, n0);
 #pragma unroll
-              for (int j = 0; j < 64; ++j) v[j] += b[j];
-            }
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
-              const float t = bf16_round(v[j]);
-              ss = fmaf(t, t, ss);
+            for (int j = 0; j < 16; ++j) {
+              pk[c][j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+              const float2 f = unpack_bf16x2(pk[c][j]);
+              ss = fmaf(f.x, f.x, ss);
+              ss = fmaf(f.y, f.y, ss);
             }
           }
-          // Publish the partial, then wait for the other tiles of this (row block, group).
-          if (row_ok) p.part[static_cast<size_t>(row) * part_cols + n_blk] = ss;
-          __threadfence();
-          __syncwarp();
+          tc_fence_before();
+          mbar_arrive(&tempty_bar[buf]);
+
+          const bool do_rope = group < p.rope_groups;
+          const float* cb = nullptr;
+          const float* sb = nullptr;
+          float cs_cur[16], sn_cur[16];
+          if (do_rope) {
+            // Pair-major tables: a warp's 32 consecutive tokens read one 128-byte line per
+            // pair. Chunk 0's entries are requested now and land during the exchange.
+            const int rr = row_ok ? row : s.M - 1;
+            const int b = rr / p.rows_per_batch;
+            const int tok = rr - b * p.rows_per_batch + p.token_offset;
+            const int pair0 = ((n_blk * BN + col_base - group * p.norm_width) & 127) >> 1;
+            cb = p.rope_cos + static_cast<size_t>(pair0) * p.rope_ld + tok;
+            sb = p.rope_sin + static_cast<size_t>(pair0) * p.rope_ld + tok;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              cs_cur[i] = __ldg(cb + static_cast<size_t>(i) * p.rope_ld);
+              sn_cur[i] = __ldg(sb + static_cast<size_t>(i) * p.rope_ld);
+            }
+          }
+
+          if (half == 1) ss_smem[r] = ss;
+          named_bar_sync(3, 2 * kEpiThreads);
           unsigned int* ctr = p.counters + m_blk * p.norm_groups + group;
-          const unsigned int target = 4u * tiles_per_group;
-          if (lane == 0) {
-            atomicAdd(ctr, 1u);
-            if (ld_acquire_gpu(ctr) < target) {
-              const uint64_t t0 = globaltimer_ns();
-              const uint64_t limit = g_wdit_wait_limit_ns;
-              while (ld_acquire_gpu(ctr) < target) {
-                if (globaltimer_ns() - t0 > limit) {
-                  report_error(kErrTimeout, kSiteExchange, static_cast<unsigned int>(tile));
-                  failed = true;
-                  break;
-                }
-                __nanosleep(64);
+          if (half == 0) {
+            // Publish: partial stores, warp barrier, then one release-increment per warp.
+            ss += ss_smem[r];
+            if (row_ok) p.part[static_cast<size_t>(row) * part_cols + n_blk] = ss;
+            __syncwarp();
+            if (lane == 0) red_release_add(ctr, 1u);
+          }
+          // Wait (one lane per warp, acquire) until every tile of the group has published.
+          bool fail_local = false;
+          if (lane == 0 && ld_acquire_gpu(ctr) < pub_target) {
+            const uint64_t t0 = globaltimer_ns();
+            const uint64_t limit = g_wdit_wait_limit_ns;
+            while (ld_acquire_gpu(ctr) < pub_target) {
+              if (globaltimer_ns() - t0 > limit) {
+                report_error(kErrTimeout, kSiteExchange, static_cast<unsigned int>(tile));
+                fail_local = true;
+                break;
               }
+              __nanosleep(20);
             }
           }
-          failed = named_bar_any(2, kEpiThreads, failed);
-          __threadfence();
+          failed = named_bar_any(3, 2 * kEpiThreads, fail_local);
+          if (failed) break;
           float tot = 0.f;
           if (row_ok) {
             const float* pr = p.part + static_cast<size_t>(row) * part_cols + group * tiles_per_group;
             for (int t = 0; t < tiles_per_group; ++t) tot += ld_cg_f32(pr + t);
           }
           rms = rsqrtf(tot / static_cast<float>(p.norm_width) + p.norm_eps);
-          __syncwarp();
-          if (lane == 0 && !failed) {
-            // Second round of arrivals: the last reader resets the counter for the next launch.
-            const unsigned int old = atomicAdd(ctr, 1u);
-            if (old == 2u * target - 1u) atomicExch(ctr, 0u);
+          pending_ctr = ctr;
+
+          // Pass 2 from registers: WanRMSNorm (bf16(bf16(x * rstd) * w)), RoPE, bf16 store of
+          // the row's 64 contiguous bytes per chunk (no inter-warp synchronization).
+          const float* wn = group == 0 ? p.norm_w[0] : p.norm_w[1];
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            const int n0 = n_blk * BN + col_base + c * 32;
+            if (do_rope && c > 0) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                cs_cur[i] = __ldg(cb + static_cast<size_t>(16 * c + i) * p.rope_ld);
+                sn_cur[i] = __ldg(sb + static_cast<size_t>(16 * c + i) * p.rope_ld);
+              }
+            }
+            float v[32];
+            const float4* wp = reinterpret_cast<const float4*>(wn + (n0 - group * p.norm_width));
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 w4 = __ldg(wp + q);
+              const float2 a = unpack_bf16x2(pk[c][2 * q]);
+              const float2 b = unpack_bf16x2(pk[c][2 * q + 1]);
+              v[4 * q] = bf16_round(bf16_round(a.x * rms) * w4.x);
+              v[4 * q + 1] = bf16_round(bf16_round(a.y * rms) * w4.y);
+              v[4 * q + 2] = bf16_round(bf16_round(b.x * rms) * w4.z);
+              v[4 * q + 3] = bf16_round(bf16_round(b.y * rms) * w4.w);
+            }
+            if (do_rope) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float e = v[2 * i], o = v[2 * i + 1];
+                v[2 * i] = e * cs_cur[i] - o * sn_cur[i];
+                v[2 * i + 1] = e * sn_cur[i] + o * cs_cur[i];
+              }
+            }
+            uint32_t w[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+            if (row_ok) {
+              uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) + (static_cast<size_t>(row) * p.ldo + n0) * 2;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) st_global_v4(dst + 16 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+            }
           }
+          continue;
         }
-        const bool do_rope = normed && group < p.rope_groups;
-        const float* wn = normed ? p.norm_w[group] : nullptr;
-        int tok = 0;
-        if (do_rope && row_ok) {
-          const int b = row / p.rows_per_batch;
-          tok = row - b * p.rows_per_batch + p.token_offset;
-        }
-        // Pass 2 (pass 1 for plain columns): finish and store.
+
+        // Plain tiles (all of gemm_act, the unnormalized column groups of the norm GEMM).
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-          const int n0 = n_blk * BN + c * 64;
-          float v[64];
-          tmem_ld32(tbase + c * 64, &v[0]);
-          tmem_ld32(tbase + c * 64 + 32, &v[32]);
-          if (c == BN / 64 - 1) {
+        for (int c = 0; c < kChunks; ++c) {
+          const int n0 = n_blk * BN + col_base + c * 32;
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          if (c == kChunks - 1) {
             tc_fence_before();
             mbar_arrive(&tempty_bar[buf]);
           }
-          if (n0 >= s.N) continue;
-          float b[64];
-          if (use_ln) {
-            load_vec64(p.ln.csum, n0, b);
+          if (n0 >= s.N) continue;  // uniform inside the half
+          finish_linear(v, n0);
+          if (KIND == kEpiAct && p.act == 1) {
 #pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] = rstd * fmaf(-mu, b[j], v[j]);
+            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
           }
-          if (p.vec != nullptr) {
-            load_vec64(p.vec, n0, b);
+          uint32_t w[16];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] += b[j];
+          for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+          // Stage 128 rows x 32 bf16 (64-byte swizzle) and store with TMA.
+          if (ht == 0) bulk_wait_read<1>();
+          named_bar_sync(bar_half, kEpiThreads);
+          const uint32_t rowa = stg_half + sbuf * kStgBytes + r * 64;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            st_shared_v4(rowa + ((q ^ ((r >> 1) & 3)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
           }
-          if (normed) {
-            load_vec64(wn, n0 - group * p.norm_width, b);
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
-              // WanRMSNorm rounding: bf16(bf16(x * rstd) * w), x the bf16 projection.
-              const float y = bf16_round(bf16_round(v[j]) * rms);
-              v[j] = bf16_round(y * b[j]);
-            }
-          }
-          if (do_rope) {
-            // Interleaved pairs (2i, 2i+1) of each 128-wide head rotated by the
-            // token's table entry i (44/42/42 frame/height/width split baked into the table).
-            const int pair0 = ((n0 - group * p.norm_width) & 127) >> 1;  // 0 or 32
-            float cs[32], sn[32];
-            if (row_ok) {
-              const float4* pc = reinterpret_cast<const float4*>(p.rope_cos + static_cast<size_t>(tok) * 64 + pair0);
-              const float4* ps = reinterpret_cast<const float4*>(p.rope_sin + static_cast<size_t>(tok) * 64 + pair0);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const float4 a = __ldg(pc + q);
-                const float4 d = __ldg(ps + q);
-                cs[4 * q] = a.x; cs[4 * q + 1] = a.y; cs[4 * q + 2] = a.z; cs[4 * q + 3] = a.w;
-                sn[4 * q] = d.x; sn[4 * q + 1] = d.y; sn[4 * q + 2] = d.z; sn[4 * q + 3] = d.w;
-              }
-            } else {
-#pragma unroll
-              for (int q = 0; q < 32; ++q) { cs[q] = 1.f; sn[q] = 0.f; }
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float e = v[2 * i], o = v[2 * i + 1];
-              v[2 * i] = e * cs[i] - o * sn[i];
-              v[2 * i + 1] = e * sn[i] + o * cs[i];
-            }
-          }
-          uint32_t w[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-          const uint32_t stg = stg0 + sbuf * 16384;
-          if (et == 0) bulk_wait_read<1>();
-          named_bar_sync(1, kEpiThreads);
-          stage_row_sw128(stg, r, w);
           fence_proxy_async_smem();
-          named_bar_sync(1, kEpiThreads);
-          if (et == 0) {
-            tma_store_2d(&tmOut, epi_base + sbuf * 16384, n0, m_blk * BM);
+          named_bar_sync(bar_half, kEpiThreads);
+          if (ht == 0) {
+            tma_store_2d(&tmOut, stg_half_ptr + sbuf * kStgBytes, n0, m_blk * BM);
             bulk_commit();
           }
           sbuf ^= 1;
         }
       }
-      if (et == 0) bulk_wait_all<0>();
-    } else {
+      if (KIND == kEpiNorm && !failed) {
+        named_bar_sync(3, 2 * kEpiThreads);
+        release_pending();
+      }
+      if (ht == 0) bulk_wait_all<0>();
+    } else if (half == 0) {
       // ----------------------------- residual -----------------------------
+      const int et = ht;
       constexpr int NB = Cfg<kEpiResidual>::kNumCBuf;
       constexpr int CPT = BN / 32;  // 32-column chunks per tile
       uint8_t* cbuf0 = epi_base;
@@ -719,6 +735,14 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, con
   }
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
+  if (max_ctas <= 0 && min_grid > 1 && s.tiles > grid) {
+    // Norm epilogue: a multiple of the group size keeps a group's tiles in one wave (no
+    // waiting on the next wave), and a grid that is not a multiple of the column-tile count
+    // rotates every CTA through normalized and plain tiles (their epilogue costs differ).
+    int g = grid - grid % min_grid;
+    while (g > min_grid && p.norm_groups * min_grid < s.n_blocks && g % s.n_blocks == 0) g -= min_grid;
+    if (g >= min_grid) grid = g;
+  }
   if (s.tiles < grid) grid = s.tiles;
   if (grid <= 0) return WDIT_OK;
   // The cross-tile exchange of the norm epilogue needs the tiles of one group on distinct,
@@ -828,7 +852,7 @@ int wdit_gemm_act(const void* A, int lda, const void* B, int ldb, void* out, int
   CUtensorMap ma, mb, mo, none;
   memset(&none, 0, sizeof(none));
   if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
-  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
   return launch<kEpiAct>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), false,
                          max_ctas);
@@ -882,19 +906,17 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
 
 long long wdit_gemm_norm_workspace_bytes(int M, int N, int norm_groups, int norm_width) {
   if (M <= 0 || norm_groups <= 0 || norm_width <= 0) return 0;
-  const long long m_blocks = (M + BM - 1) / BM;
   const long long part_cols = static_cast<long long>(norm_groups) * (norm_width / BN);
   const long long part = ((static_cast<long long>(M) * part_cols * 4 + 255) / 256) * 256;
-  const long long ctr = ((m_blocks * norm_groups * 4 + 255) / 256) * 256;
   (void)N;
-  return part + ctr;
+  return kCounterRegionBytes + part;
 }
 
 int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
                    const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
                    int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
                    const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos, const float* rope_sin,
-                   int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes, void* stream,
+                   int rope_ld, int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes, void* stream,
                    int max_ctas) {
   int rc = check_common(A, lda, B, ldb, M, N, K);
   if (rc) return rc;
@@ -910,6 +932,7 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
   }
   if (rope_groups > 0) {
     if (rope_cos == nullptr || rope_sin == nullptr || rows_per_batch <= 0 || token_offset < 0) return WDIT_ERR_ARG;
+    if (rope_ld < rows_per_batch + token_offset) return WDIT_ERR_SHAPE;
     if (!aligned16(rope_cos) || !aligned16(rope_sin)) return WDIT_ERR_ALIGN;
     if (norm_width % 128 != 0) return WDIT_ERR_SHAPE;
   }
@@ -926,19 +949,21 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
   p.rope_groups = rope_groups;
   p.rope_cos = rope_cos;
   p.rope_sin = rope_sin;
+  p.rope_ld = rope_ld;
   p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
   p.token_offset = token_offset;
   p.has_out_map = 1;
+  p.out = out;
+  p.ldo = ldo;
   if (norm_groups > 0) {
-    const long long part_cols = static_cast<long long>(norm_groups) * (norm_width / BN);
-    const long long part = ((static_cast<long long>(M) * part_cols * 4 + 255) / 256) * 256;
-    p.part = reinterpret_cast<float*>(workspace);
-    p.counters = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(workspace) + part);
+    if (static_cast<long long>((M + BM - 1) / BM) * norm_groups * 4 > kCounterRegionBytes) return WDIT_ERR_SHAPE;
+    p.counters = reinterpret_cast<unsigned int*>(workspace);
+    p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kCounterRegionBytes);
   }
   CUtensorMap ma, mb, mo, none;
   memset(&none, 0, sizeof(none));
   if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
-  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
   return launch<kEpiNorm>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
                           norm_groups > 0, max_ctas, norm_groups > 0 ? norm_width / BN : 1);
@@ -1005,7 +1030,8 @@ int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* 
                           const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
                           int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
                           const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
-                          const float* rope_sin, int rows_per_batch, int token_offset, void* stream, int max_ctas) {
+                          const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream,
+                          int max_ctas) {
   int rc = check_common(A, lda, B, ldb, M, N, K);
   if (rc) return rc;
   if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
@@ -1015,6 +1041,7 @@ int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* 
   if (!aligned16(norm_w0) || (norm_w1 && !aligned16(norm_w1))) return WDIT_ERR_ALIGN;
   if (rope_groups > 0) {
     if (rope_cos == nullptr || rope_sin == nullptr || rows_per_batch <= 0 || token_offset < 0) return WDIT_ERR_ARG;
+    if (rope_ld < rows_per_batch + token_offset) return WDIT_ERR_SHAPE;
     if (!aligned16(rope_cos) || !aligned16(rope_sin)) return WDIT_ERR_ALIGN;
     if (norm_width % 128 != 0) return WDIT_ERR_SHAPE;
   }
@@ -1036,14 +1063,16 @@ int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* 
   p.rope_groups = rope_groups;
   p.rope_cos = rope_cos;
   p.rope_sin = rope_sin;
+  p.rope_ld = rope_ld;
   p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
   p.token_offset = token_offset;
   p.has_out_map = 1;
-  const long long part_cols = static_cast<long long>(norm_groups) * (norm_width / BN);
-  const long long part_bytes = ((static_cast<long long>(M) * part_cols * 4 + 255) / 256) * 256;
-  const long long ctr_bytes = need - part_bytes;
-  p.part = reinterpret_cast<float*>(scratch);
-  p.counters = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(scratch) + part_bytes);
+  p.out = out;
+  p.ldo = ldo;
+  const long long ctr_bytes = static_cast<long long>((M + BM - 1) / BM) * norm_groups * 4;
+  if (ctr_bytes > kCounterRegionBytes) return WDIT_ERR_SHAPE;
+  p.counters = reinterpret_cast<unsigned int*>(scratch);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCounterRegionBytes);
   // The counters start every launch at zero (the array keeps whatever the last call left).
   cudaError_t e = cudaMemsetAsync(p.counters, 0, static_cast<size_t>(ctr_bytes), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
@@ -1051,7 +1080,7 @@ int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* 
   CUtensorMap ma, mb, mo, none;
   memset(&none, 0, sizeof(none));
   if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
-  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
   return launch<kEpiNorm>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), true,
                           max_ctas, norm_width / BN);

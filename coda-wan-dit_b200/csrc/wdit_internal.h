@@ -37,9 +37,12 @@ struct EpiParams {
   int rope_groups;  // leading groups that also get 3D RoPE
   const float* rope_cos;
   const float* rope_sin;
+  int rope_ld;  // pair-major tables: entry (pair, token) at pair * rope_ld + token
   int token_offset;
   float* part;             // scratch [M, norm_groups * norm_width/256]
   unsigned int* counters;  // scratch [m_blocks * norm_groups], zero between launches
+  void* out;  // norm epilogue: direct bf16 stores
+  int ldo;
   int has_out_map;
   int has_x_map;
 };

@@ -170,7 +170,10 @@ def _ws_for(device) -> Workspace:
 def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_width=0, norm_w=(None, None),
               norm_eps=1e-6, rope_groups=0, rope_cos=None, rope_sin=None, rows_per_batch=0, token_offset=0,
               out=None, workspace: Workspace | None = None, max_ctas=0):
-    """out[M,N] bf16 = RoPE(RMSNorm_fullwidth(bf16(LN(a @ w.T) + vec))) per column group."""
+    """out[M,N] bf16 = RoPE(RMSNorm_fullwidth(bf16(LN(a @ w.T) + vec))) per column group.
+
+    rope_cos / rope_sin are pair-major [64, T] fp32 tables (row = rotary pair, column = token).
+    """
     _require_cuda(a, w)
     a = _rowmajor(a)
     M, K = a.shape
@@ -186,11 +189,16 @@ def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_w
     w0 = _f32vec(norm_w[0]) if norm_groups > 0 else None
     w1 = _f32vec(norm_w[1]) if norm_groups > 1 else None
     vec = _f32vec(vec)
+    rope_ld = 0
+    if rope_groups > 0:
+        assert rope_cos.shape == rope_sin.shape and rope_cos.shape[0] == HEAD_DIM // 2
+        assert rope_cos.is_contiguous() and rope_sin.is_contiguous() and rope_cos.dtype == torch.float32
+        rope_ld = rope_cos.shape[1]
     call(
         "wdit_gemm_norm",
         ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(out), out.stride(0), M, N, K,
         ptr(vec), *_ln_args(ln, K), norm_groups, norm_width, ptr(w0), ptr(w1), float(norm_eps),
-        rope_groups, ptr(rope_cos), ptr(rope_sin), rows_per_batch, token_offset, ptr(ws), nbytes,
+        rope_groups, ptr(rope_cos), ptr(rope_sin), rope_ld, rows_per_batch, token_offset, ptr(ws), nbytes,
         stream_ptr(), max_ctas,
     )
     return out
@@ -305,7 +313,7 @@ def qk_coda_rms_rope(a, qk_weight_kn, qk_bias, q_weight, k_weight, cos, sin, eps
     assert cos.shape == sin.shape == (m, HEAD_DIM // 2)
     qk = gemm_norm(
         a, _weight_nk(qk_weight_kn), vec=qk_bias, norm_groups=2, norm_width=DIM, norm_w=(q_weight, k_weight),
-        norm_eps=eps, rope_groups=2, rope_cos=cos.float().contiguous(), rope_sin=sin.float().contiguous(),
+        norm_eps=eps, rope_groups=2, rope_cos=cos.float().t().contiguous(), rope_sin=sin.float().t().contiguous(),
         rows_per_batch=m, token_offset=0,
     )
     return qk[:, :DIM], qk[:, DIM:]
@@ -325,16 +333,28 @@ def rmsnorm_fused(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Te
     return out.view(shape)
 
 
-def build_wan_rope_table(grid_fhw, freqs: torch.Tensor):
-    """Shared per-token cos/sin [f*h*w, 64] fp32 tables.  wan_coda_kernels.py:414-430."""
+def _rope_table(grid_fhw, freqs: torch.Tensor, pair_major: bool):
     f, h, w = (int(v) for v in grid_fhw)
     _require_cuda(freqs)
     assert freqs.dim() == 2 and freqs.shape[1] == HEAD_DIM // 2 and freqs.is_complex()
     fr = torch.view_as_real(freqs.to(torch.complex128).contiguous()).contiguous()
-    cos = torch.empty((f * h * w, HEAD_DIM // 2), dtype=torch.float32, device=freqs.device)
+    shape = (HEAD_DIM // 2, f * h * w) if pair_major else (f * h * w, HEAD_DIM // 2)
+    cos = torch.empty(shape, dtype=torch.float32, device=freqs.device)
     sin = torch.empty_like(cos)
-    call("wdit_rope_table", ptr(fr), freqs.shape[0], f, h, w, ptr(cos), ptr(sin), stream_ptr())
+    call("wdit_rope_table", ptr(fr), freqs.shape[0], f, h, w, 1 if pair_major else 0, ptr(cos), ptr(sin),
+         stream_ptr())
     return cos, sin
+
+
+def build_wan_rope_table(grid_fhw, freqs: torch.Tensor):
+    """Shared per-token cos/sin [f*h*w, 64] fp32 tables.  wan_coda_kernels.py:414-430."""
+    return _rope_table(grid_fhw, freqs, pair_major=False)
+
+
+def build_rope_table_pair_major(grid_fhw, freqs: torch.Tensor):
+    """The same tables transposed to [64, f*h*w] (what the fused QKV epilogue reads: a warp's
+    consecutive tokens load one contiguous line per rotary pair)."""
+    return _rope_table(grid_fhw, freqs, pair_major=True)
 
 
 def replace_parameter_with_view(module: nn.Module, name: str, view: torch.Tensor) -> None:

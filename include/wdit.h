@@ -85,15 +85,17 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
                        int gate_b_stride, int rows_per_batch, void* x_bf16_out, int ldx, float* stats_out,
                        void* stream, int max_ctas);
 
-/* Workspace bytes wdit_gemm_norm needs (partials + arrival counters). The counter part must be
- * zero before the first launch; the kernel leaves it zero after every successful launch. */
+/* Workspace bytes wdit_gemm_norm needs: a fixed 64 KiB region of arrival counters at offset 0
+ * (zero before the first launch; every successful launch leaves it zero, so one workspace can
+ * serve launches of any shape) followed by the per-row partials. */
 long long wdit_gemm_norm_workspace_bytes(int M, int N, int norm_groups, int norm_width);
 
 /*
  * out[M,N] (bf16): y = LN(A . B^T) + vec, rounded to bf16; columns [g*W, (g+1)*W) for
  * g < norm_groups get the full-width WanRMSNorm bf16(bf16(y * rsqrt(mean_W(y^2) + eps)) * w_g),
- * and for g < rope_groups the interleaved-pair 3D RoPE with rope_cos/sin[token, 64] where
- * token = m % rows_per_batch + token_offset. Remaining columns are stored as bf16(y).
+ * and for g < rope_groups the interleaved-pair 3D RoPE with the pair-major tables
+ * rope_cos/sin[pair * rope_ld + token] (pair < 64, token = m % rows_per_batch + token_offset,
+ * rope_ld >= rows_per_batch + token_offset). Remaining columns are stored as bf16(y).
  * QKV: norm_groups 2, rope_groups 2; cross-Q: 1, 0; cross-KV: 1, 0.
  * Replaces: coda_wan/wan_coda_kernels.py:355-368 qk_coda_rms_rope (= :192-230
  * qk_linear_bias_partial_rms + :313-352 qk_rms_rope_from_partials), the V projection at
@@ -103,8 +105,8 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
                    const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
                    int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
                    const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos, const float* rope_sin,
-                   int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes, void* stream,
-                   int max_ctas);
+                   int rope_ld, int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes,
+                   void* stream, int max_ctas);
 
 /*
  * wdit_gemm_norm without a workspace argument: it allocates nothing and takes no scratch from
@@ -114,7 +116,7 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
  * Same arguments and result as wdit_gemm_norm (norm_groups >= 1). The row-statistics scratch
  * is a fixed array of WDIT_STATIC_SCRATCH_BYTES (4 MiB) per GPU, held for the life of the
  * process; problems needing more (wdit_gemm_norm_workspace_bytes > 4 MiB, e.g. QKV beyond
- * ~87k rows) return WDIT_ERR_SCRATCH_LIMIT. Every call on a device shares that array: calls
+ * ~86k rows) return WDIT_ERR_SCRATCH_LIMIT. Every call on a device shares that array: calls
  * that overlap on the GPU race. Each call zeroes the array's counters on `stream` first. The
  * first call on a device looks the array's address up (with this library's current device,
  * see wdit_set_device); make it before any stream capture.
@@ -123,7 +125,8 @@ int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* 
                           const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
                           int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
                           const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
-                          const float* rope_sin, int rows_per_batch, int token_offset, void* stream, int max_ctas);
+                          const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream,
+                          int max_ctas);
 
 /* Bytes of the static scratch array of wdit_gemm_norm_static (= WDIT_STATIC_SCRATCH_BYTES). */
 long long wdit_static_scratch_bytes(void);
@@ -177,13 +180,15 @@ int wdit_qk_rms_rope_from_partials(void* qk, int ldqk, const float* partial, int
                                    void* stream);
 
 /*
- * cos/sin[f*h*w, 64] (fp32) of the 3D RoPE for grid (f, h, w), from the per-axis complex
+ * cos/sin (fp32) of the 3D RoPE for grid (f, h, w), T = f*h*w tokens, from the per-axis complex
  * frequency table freqs[max_pos, 64] (complex128 stored as interleaved fp64 (re, im) pairs);
- * the 64 columns split [22, 21, 21] between the frame, height and width axes.
+ * the 64 pairs split [22, 21, 21] between the frame, height and width axes. Layout: token-major
+ * [T, 64] (pair_major = 0, the reference's layout) or pair-major [64, T] (pair_major = 1, what
+ * wdit_gemm_norm reads).
  * Replaces: coda_wan/wan_coda_kernels.py:414-430 build_wan_rope_table.
  */
-int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, float* cos_out, float* sin_out,
-                    void* stream);
+int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, int pair_major, float* cos_out,
+                    float* sin_out, void* stream);
 
 /*
  * Mean of squares of x[M,N] (bf16) over consecutive column blocks: out[M, N/block] (fp32).

@@ -159,8 +159,9 @@ def attention(q, k, v, k_lens, cd):
     Lk = k.shape[1]
     mask = None
     if k_lens is not None:
-        kl = torch.as_tensor(k_lens, device=q.device).view(B, 1, 1, 1)
-        if bool((kl < Lk).any()):
+        kl_host = torch.as_tensor(k_lens).cpu()  # host copy: no device sync when k_lens is on the CPU
+        if bool((kl_host < Lk).any()):
+            kl = kl_host.to(q.device).view(B, 1, 1, 1)
             mask = torch.arange(Lk, device=q.device).view(1, 1, 1, Lk) < kl
     o = F.scaled_dot_product_attention(
         q.to(cd).transpose(1, 2), k.to(cd).transpose(1, 2), v.to(cd).transpose(1, 2), attn_mask=mask

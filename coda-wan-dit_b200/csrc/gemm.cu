@@ -65,7 +65,7 @@ constexpr int kTmemCols = 2 * BN;  // two accumulator buffers
 // different shapes can share one workspace (partials never overwrite counters).
 constexpr long long kCounterRegionBytes = 64 * 1024;
 
-enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiNorm = 2 };
+enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiNorm = 2, kEpiResidualLongK = 3 };
 
 template <int KIND>
 struct Cfg;
@@ -84,11 +84,27 @@ struct Cfg<kEpiNorm> {
   static constexpr int kNumCBuf = 0;
   static constexpr int kEpiArrivals = 2 * kEpiThreads;
 };
+// Residual epilogues stream the fp32 residual through a ring of 128-row x 32-column fp32
+// tiles (16 KB, 128-byte swizzle): TMA load, in-place update, TMA store. kLookahead chunks
+// are requested ahead of the one being processed.
+//   short K (self-O, cross-O; HBM-bound): deeper ring, 3 mainloop stages
+//   long K  (FFN2; tensor-bound): 4 mainloop stages, shallow ring
 template <>
 struct Cfg<kEpiResidual> {
   static constexpr int kStages = 3;
-  static constexpr int kNumCBuf = 4;  // 128 rows x 32 fp32 (16 KB) residual/out ring
-  static constexpr uint32_t kEpiBytes = kNumCBuf * 16384 + 2 * 8192;  // + 2 x (128 x 32 bf16)
+  static constexpr int kNumCBuf = 4;
+  static constexpr int kLookahead = 2;
+  static constexpr bool kXStaged = true;  // bf16 copy staged (64-byte swizzle) + TMA store
+  static constexpr uint32_t kEpiBytes = kNumCBuf * 16384 + 2 * kStgBytes;
+  static constexpr int kEpiArrivals = kEpiThreads;
+};
+template <>
+struct Cfg<kEpiResidualLongK> {
+  static constexpr int kStages = 4;
+  static constexpr int kNumCBuf = 2;
+  static constexpr int kLookahead = 1;
+  static constexpr bool kXStaged = false;  // bf16 copy stored from registers
+  static constexpr uint32_t kEpiBytes = kNumCBuf * 16384;
   static constexpr int kEpiArrivals = kEpiThreads;
 };
 
@@ -169,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull_bar = bars + 2 * STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* cload_bar = tempty_bar + 2;  // kNumCBuf entries (residual only)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cload_bar + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cload_bar + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -183,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull_bar[i], 1);
       mbar_init(&tempty_bar[i], Cfg<KIND>::kEpiArrivals);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&cload_bar[i], 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&cload_bar[i], 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -520,8 +536,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (half == 0) {
       // ----------------------------- residual -----------------------------
       const int et = ht;
-      constexpr int NB = Cfg<kEpiResidual>::kNumCBuf;
+      constexpr int NB = Cfg<KIND>::kNumCBuf;
+      constexpr int LA = Cfg<KIND>::kLookahead;
+      static_assert(LA >= 1 && LA < NB, "lookahead must leave one buffer being stored");
       constexpr int CPT = BN / 32;  // 32-column chunks per tile
+      constexpr bool XS = Cfg<KIND>::kXStaged;
       uint8_t* cbuf0 = epi_base;
       uint8_t* xbuf0 = epi_base + NB * 16384;
       const int my_tiles = (blockIdx.x < s.tiles) ? (s.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -540,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(cbuf0 + (g % NB) * 16384, &tmC, bar, n0 < s.N ? n0 : 0, m_blk * BM);
       };
       if (et == 0) {
-        for (int g = 0; g < 2 && g < total_chunks; ++g) issue_load(g);
+        for (int g = 0; g < LA && g < total_chunks; ++g) issue_load(g);
       }
       int g = 0;
       bool failed = false;
@@ -563,8 +582,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < CPT; ++c, ++g) {
           const int n0 = n_blk * BN + c * 32;
           if (et == 0) {
-            bulk_wait_read<1>();
-            if (g + 2 < total_chunks) issue_load(g + 2);
+            // Buffer of chunk g+LA last held chunk g+LA-NB: its store must have been read.
+            bulk_wait_read<NB - LA - 1>();
+            if (g + LA < total_chunks) issue_load(g + LA);
           }
           named_bar_sync(1, kEpiThreads);
           float acc[32];
@@ -614,30 +634,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                          __float_as_uint(out[4 * q + 2]), __float_as_uint(out[4 * q + 3]));
           }
           if (col_ok && p.stats_out != nullptr) {
-            // Chunk (mean, M2), merged into the running per-row statistics (Chan).
-            float sum = 0.f;
+            // Chunk (mean, M2), merged into the running per-row statistics (Chan). Four
+            // independent accumulators keep the dependency chains short.
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int j = 0; j < 32; ++j) sum += out[j];
-            const float cmean = sum * (1.f / 32.f);
-            float cm2 = 0.f;
+            for (int j = 0; j < 32; ++j) s4[j & 3] += out[j];
+            const float cmean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / 32.f);
+            float m4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float d = out[j] - cmean;
-              cm2 = fmaf(d, d, cm2);
+              m4[j & 3] = fmaf(d, d, m4[j & 3]);
             }
+            const float cm2 = (m4[0] + m4[1]) + (m4[2] + m4[3]);
             const float tot = run_n + 32.f;
             const float delta = cmean - run_mean;
             run_mean += delta * (32.f / tot);
             run_m2 += cm2 + delta * delta * (run_n * 32.f / tot);
             run_n = tot;
           }
-          const uint32_t xrow = smem_u32(xbuf0 + (g & 1) * 8192) + r * 64;
-          if (has_x) {
+          if (XS && has_x) {
+            const uint32_t xrow = smem_u32(xbuf0 + (g & 1) * kStgBytes) + r * 64;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               st_shared_v4(xrow + ((q ^ ((r >> 1) & 3)) << 4), pack_bf16x2(out[8 * q], out[8 * q + 1]),
                            pack_bf16x2(out[8 * q + 2], out[8 * q + 3]), pack_bf16x2(out[8 * q + 4], out[8 * q + 5]),
                            pack_bf16x2(out[8 * q + 6], out[8 * q + 7]));
+            }
+          }
+          if (!XS && has_x && col_ok && row < s.M) {
+            // bf16 copy of the updated row chunk, stored straight from registers (64 bytes).
+            uint8_t* dst = reinterpret_cast<uint8_t*>(p.x_out) + (static_cast<size_t>(row) * p.ldx + n0) * 2;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              st_global_v4(dst + 16 * q, pack_bf16x2(out[8 * q], out[8 * q + 1]), pack_bf16x2(out[8 * q + 2], out[8 * q + 3]),
+                           pack_bf16x2(out[8 * q + 4], out[8 * q + 5]), pack_bf16x2(out[8 * q + 6], out[8 * q + 7]));
             }
           }
           fence_proxy_async_smem();
@@ -648,7 +679,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (et == 0) {
             if (col_ok) {
               tma_store_2d(&tmOut, cbuf0 + (g % NB) * 16384, n0, m_blk * BM);
-              if (has_x) tma_store_2d(&tmX, xbuf0 + (g & 1) * 8192, n0, m_blk * BM);
+              if (XS && has_x) tma_store_2d(&tmX, xbuf0 + (g & 1) * kStgBytes, n0, m_blk * BM);
             }
             bulk_commit();
           }
@@ -662,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (et == 0) bulk_wait_all<0>();
       // Do not leave with residual loads in flight (only reachable after a failure).
       if (failed && et == 0) {
-        for (int gg = g; gg <= g + 2 && gg < total_chunks; ++gg) wait_parity(&cload_bar[gg % NB], (gg / NB) & 1, kSiteDrain);
+        for (int gg = g; gg <= g + LA && gg < total_chunks; ++gg) wait_parity(&cload_bar[gg % NB], (gg / NB) & 1, kSiteDrain);
       }
     }
   }
@@ -890,6 +921,8 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
   p.stats_out = stats_out;
   p.has_out_map = 1;
   p.has_x_map = x_bf16_out != nullptr ? 1 : 0;
+  p.x_out = x_bf16_out;
+  p.ldx = ldx;
   CUtensorMap ma, mb, mo, mc, mx;
   memset(&mx, 0, sizeof(mx));
   if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
@@ -897,9 +930,15 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
     return rc;
   if ((rc = make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, N, M, ldc, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
+  if (x_bf16_out != nullptr && (reinterpret_cast<uintptr_t>(x_bf16_out) & 15) != 0) return WDIT_ERR_ALIGN;
+  if (x_bf16_out != nullptr && (ldx % 8) != 0) return WDIT_ERR_ALIGN;
   if (x_bf16_out != nullptr &&
       (rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x_bf16_out, N, M, ldx, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
+  // Long reductions are tensor-bound (deeper mainloop), short ones HBM-bound (deeper ring).
+  if (K >= 4096)
+    return launch<kEpiResidualLongK>(ma, mb, mo, mc, mx, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
+                                     false, max_ctas);
   return launch<kEpiResidual>(ma, mb, mo, mc, mx, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), false,
                               max_ctas);
 }

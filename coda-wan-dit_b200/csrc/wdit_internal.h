@@ -43,6 +43,8 @@ struct EpiParams {
   unsigned int* counters;  // scratch [m_blocks * norm_groups], zero between launches
   void* out;  // norm epilogue: direct bf16 stores
   int ldo;
+  void* x_out;  // residual epilogue: bf16 copy of the result (direct stores)
+  int ldx;
   int has_out_map;
   int has_x_map;
 };

@@ -268,7 +268,9 @@ class FusedWanModel(nn.Module):
         return outs
 
     # -- forward -----------------------------------------------------------
-    def forward(self, x_list, t, context_list, seq_len, text_len: int = 512):
+    def forward(self, x_list, t, context_list, seq_len, text_len: int = 512, return_tokens: bool = False):
+        """Stock signature. With token sharding (or return_tokens=True) the result is the head's
+        per-token output [B, L(local), prod(patch) * out_dim] instead of unpatchified latents."""
         dev = self.model.patch_embedding.weight.device
         B = len(x_list)
         t = torch.as_tensor(t).reshape(-1)
@@ -297,6 +299,6 @@ class FusedWanModel(nn.Module):
         x32 = x.reshape(B * Lx, self.dim)
         carried = self.carry.get(x32)
         y = self.head(x32, e, carried, B * Lx, shared_e)
-        if sp is not None:
+        if sp is not None or return_tokens:
             return y.view(B, Lx, -1)
         return [u.float() for u in self.unpatchify(y, grids, lens, Lx)]

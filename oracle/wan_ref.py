@@ -153,15 +153,20 @@ def rope_apply(x: torch.Tensor, grids: list[tuple[int, int, int]], freqs: torch.
     return out
 
 
+def _host_list(v):
+    """Python values of a small tensor / sequence (no device-side compute)."""
+    return v.tolist() if torch.is_tensor(v) else list(v)
+
+
 def attention(q, k, v, k_lens, cd):
     """q [B, Lq, H, hd], k/v [B, Lk, H, hd]; softmax(q k^T / sqrt(hd)) v with keys >= k_lens masked."""
     B, Lq, H, hd = q.shape
     Lk = k.shape[1]
     mask = None
     if k_lens is not None:
-        kl_host = torch.as_tensor(k_lens).cpu()  # host copy: no device sync when k_lens is on the CPU
-        if bool((kl_host < Lk).any()):
-            kl = kl_host.to(q.device).view(B, 1, 1, 1)
+        lens = _host_list(k_lens)
+        if any(int(v) < Lk for v in lens):
+            kl = torch.tensor([int(v) for v in lens], device=q.device).view(B, 1, 1, 1)
             mask = torch.arange(Lk, device=q.device).view(1, 1, 1, Lk) < kl
     o = F.scaled_dot_product_attention(
         q.to(cd).transpose(1, 2), k.to(cd).transpose(1, 2), v.to(cd).transpose(1, 2), attn_mask=mask
@@ -234,7 +239,7 @@ class WanBlockRef(nn.Module):
 
     def forward(self, x, e, seq_lens, grid_sizes, freqs, context, context_lens):
         cd = self.compute_dtype
-        grids = [tuple(int(v) for v in g) for g in torch.as_tensor(grid_sizes).tolist()]
+        grids = [tuple(int(v) for v in g) for g in _host_list(grid_sizes)]
         e = (self.modulation.float() + e.float()).chunk(6, dim=1)
         y = self.self_attn(self.norm1(x).float() * (1 + e[1]) + e[0], seq_lens, grids, freqs, cd)
         x = x + y * e[2]
@@ -251,8 +256,8 @@ class WanBlockRef(nn.Module):
 def sinusoidal_embedding(dim: int, pos: torch.Tensor) -> torch.Tensor:
     half = dim // 2
     p = pos.to(torch.float64)
-    freq = torch.pow(torch.tensor(10000.0, dtype=torch.float64), -torch.arange(half, dtype=torch.float64) / half)
-    s = torch.outer(p, freq.to(p.device))
+    freq = torch.pow(10000.0, -torch.arange(half, dtype=torch.float64, device=p.device) / half)
+    s = torch.outer(p, freq)
     return torch.cat([torch.cos(s), torch.sin(s)], dim=1)
 
 
@@ -293,9 +298,9 @@ class WanModelRef(nn.Module):
         cfg = self.cfg
         xs = [F.conv3d(u.unsqueeze(0).to(cd), self.patch_embedding.weight.to(cd), self.patch_embedding.bias.to(cd),
                        stride=cfg.patch) for u in x_list]
-        grids = [tuple(u.shape[2:]) for u in xs]
+        grids = [tuple(int(d) for d in u.shape[2:]) for u in xs]
         xs = [u.flatten(2).transpose(1, 2) for u in xs]
-        seq_lens = torch.tensor([u.shape[1] for u in xs], dtype=torch.long)
+        seq_lens = [int(u.shape[1]) for u in xs]
         x = torch.cat([torch.cat([u, u.new_zeros(1, seq_len - u.shape[1], u.shape[2])], dim=1) for u in xs])
         tt = torch.as_tensor(t, device=x.device).reshape(-1)
         e = self.time_embedding.float()(sinusoidal_embedding(cfg.freq_dim, tt).float())
@@ -317,9 +322,8 @@ class WanModelRef(nn.Module):
 
     def forward(self, x_list, t, context_list, seq_len):
         x, e, e0, seq_lens, grids, context = self.embed(x_list, t, context_list, seq_len)
-        grid_sizes = torch.tensor(grids, dtype=torch.long)
         for blk in self.blocks:
-            x = blk(x, e0, seq_lens, grid_sizes, self.freqs, context, None)
+            x = blk(x, e0, seq_lens, grids, self.freqs, context, None)
         x = self.head(x, e, self.compute_dtype)
         return [u.float() for u in self.unpatchify(x, grids)]
 

@@ -120,3 +120,15 @@ def test_model_forward_matches_oracle(pkg):
     for g, w in zip(got, want):
         assert g.shape == w.shape
         assert rel_l2(g, w) <= 2e-2
+
+
+def test_block_14b_shape(pkg):
+    """Config 4 block shape (dim 5120, 40 heads, ffn 13824): 20-tile RMSNorm groups."""
+    cfg = wan_ref.WAN_14B
+    ref, stock, fused = make_pair(pkg, seed=41, cfg=cfg)
+    inp = wan_ref.block_inputs(cfg, (1, 12, 16), 2, seed=42, ctx_len=64, device=DEV)
+    inp["e"] = inp["e"][:1].expand(2, -1, -1).contiguous()
+    freqs = wan_ref.rope_freqs(1024, cfg.head_dim).to(DEV)
+    want = run(ref, inp, freqs)
+    got = run(fused, inp, freqs, e=inp["e"][:1], ctx_dtype=torch.bfloat16)
+    assert rel_l2(got, want) <= 1e-2 and max_abs(got, want) <= 5e-2

@@ -41,6 +41,7 @@ _SIGNATURES = {
     "wdit_stats_tile_width": (c_int, []),
     "wdit_set_wait_limit_ns": (c_int, [c_ulonglong]),
     "wdit_read_error": (c_int, [P, I]),
+    "wdit_wait_selftest": (c_int, [P, P]),
     "wdit_gemm_act": (c_int, [P, I, P, I, P, I, I, I, I, P, I, P, P, I, I, F, P, I]),
     "wdit_gemm_residual": (c_int, [P, I, P, I, P, I, P, I, I, I, I, P, P, P, I, I, P, I, P, P, I]),
     "wdit_gemm_norm_workspace_bytes": (c_longlong, [I, I, I, I]),

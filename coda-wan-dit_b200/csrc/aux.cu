@@ -98,6 +98,19 @@ __global__ void __launch_bounds__(256) ln_stats_kernel(const void* __restrict__ 
   }
 }
 
+// 8 consecutive fp32 of an optional vector (zeros when absent), two 16-byte loads.
+__device__ __forceinline__ void load_vec8(const float* __restrict__ v, int k0, float (&out)[8]) {
+  if (v == nullptr) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = 0.f;
+    return;
+  }
+  const float4 x = __ldg(reinterpret_cast<const float4*>(v + k0));
+  const float4 y = __ldg(reinterpret_cast<const float4*>(v + k0) + 1);
+  out[0] = x.x; out[1] = x.y; out[2] = x.z; out[3] = x.w;
+  out[4] = y.x; out[5] = y.y; out[6] = y.z; out[7] = y.w;
+}
+
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
     fold_weight_kernel(const __nv_bfloat16* __restrict__ W, int ldw, int N, int K, float mult_c,
@@ -111,15 +124,16 @@ __global__ void __launch_bounds__(256)
   for (int k0 = lane * 8; k0 < K; k0 += 256) {
     float w[8];
     load8(W, true, static_cast<size_t>(n) * ldw + k0, w);
+    float a8[8], b8[8], s8[8], t8[8];
+    load_vec8(ma, k0, a8);
+    load_vec8(mb, k0, b8);
+    load_vec8(sa, k0, s8);
+    load_vec8(sb, k0, t8);
     float m[8], sh[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float a = ma != nullptr ? __ldg(ma + k0 + i) : 0.f;
-      const float b = mb != nullptr ? __ldg(mb + k0 + i) : 0.f;
-      m[i] = mult_c + (a + b);
-      const float s0 = sa != nullptr ? __ldg(sa + k0 + i) : 0.f;
-      const float s1 = sb != nullptr ? __ldg(sb + k0 + i) : 0.f;
-      sh[i] = s0 + s1;
+      m[i] = mult_c + (a8[i] + b8[i]);
+      sh[i] = s8[i] + t8[i];
     }
     float wf[8];
 #pragma unroll
@@ -297,6 +311,8 @@ int wdit_fold_weight(const void* W, int ldw, int N, int K, float mult_c, const f
   if (W == nullptr || W_out == nullptr || csum_out == nullptr || vec_out == nullptr) return WDIT_ERR_ARG;
   if (N <= 0 || K <= 0 || K % 8 != 0 || ldw < K || ldw_out < K) return WDIT_ERR_SHAPE;
   if (!a16(W) || !a16(W_out) || ldw % 8 != 0 || ldw_out % 8 != 0) return WDIT_ERR_ALIGN;
+  if ((mult_a && !a16(mult_a)) || (mult_b && !a16(mult_b)) || (shift_a && !a16(shift_a)) || (shift_b && !a16(shift_b)))
+    return WDIT_ERR_ALIGN;
   fold_weight_kernel<<<row_blocks(N), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(W), ldw, N, K, mult_c, mult_a, mult_b, shift_a, shift_b, bias,
       reinterpret_cast<__nv_bfloat16*>(W_out), ldw_out, csum_out, vec_out);

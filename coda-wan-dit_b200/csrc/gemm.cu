@@ -706,6 +706,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Self-test of the bounded-wait path: one thread waits for `flag` to become nonzero with the
+// library's wait limit; when nothing sets it the wait gives up, records kErrTimeout /
+// kSiteSelfTest in the error record and the kernel returns normally.
+__global__ void wait_selftest_kernel(const unsigned int* flag) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = g_wdit_wait_limit_ns;
+  while (ld_acquire_gpu(flag) == 0u) {
+    if (globaltimer_ns() - t0 > limit) {
+      report_error(kErrTimeout, kSiteSelfTest, 0u);
+      return;
+    }
+    __nanosleep(1000);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -849,6 +865,13 @@ int wdit_num_sms(void) { return num_sms(); }
 
 int wdit_set_wait_limit_ns(unsigned long long ns) {
   cudaError_t e = cudaMemcpyToSymbol(g_wdit_wait_limit_ns, &ns, sizeof(ns));
+  return e == cudaSuccess ? WDIT_OK : WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+}
+
+int wdit_wait_selftest(const unsigned int* flag, void* stream) {
+  if (flag == nullptr) return WDIT_ERR_ARG;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag);
+  const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? WDIT_OK : WDIT_ERR_CUDA_BASE + static_cast<int>(e);
 }
 

@@ -30,6 +30,7 @@ enum ErrSite : unsigned int {
   kSiteEpiCLoad = 5,
   kSiteExchange = 6,
   kSiteDrain = 7,
+  kSiteSelfTest = 8,
 };
 constexpr unsigned int kErrTimeout = 0x7117;
 

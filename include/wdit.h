@@ -54,6 +54,11 @@ int wdit_stats_tile_width(void);
 /* Upper bound, in nanoseconds, of every device-side wait (default 2 s). */
 int wdit_set_wait_limit_ns(unsigned long long ns);
 
+/* Failure-detection self-test: a one-thread kernel waits (bounded by the wait limit) for
+ * *flag to become nonzero; if nothing sets it, the wait gives up and records
+ * {0x7117 (timeout), 8 (self-test site)} in the error record, leaving the context usable. */
+int wdit_wait_selftest(const unsigned int* flag, void* stream);
+
 /* Synchronizes the device and copies the device error record
  * {code, site, block, extra} into out4 (all zero = no error); clear != 0 resets it. */
 int wdit_read_error(unsigned int* out4, int clear);

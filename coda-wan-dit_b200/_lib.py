@@ -37,6 +37,7 @@ I = c_int
 # name -> (restype, argtypes); must match include/wdit.h
 _SIGNATURES = {
     "wdit_num_sms": (c_int, []),
+    "wdit_set_cta_pair": (c_int, [I]),
     "wdit_set_device": (c_int, [I]),
     "wdit_stats_tile_width": (c_int, []),
     "wdit_set_wait_limit_ns": (c_int, [c_ulonglong]),

@@ -59,6 +59,9 @@ constexpr uint32_t kStgBytes = 8192;  // 128 rows x 32 bf16 output staging tile
 constexpr uint32_t kTileABytes = BM * BK * 2;  // 16 KB
 constexpr uint32_t kTileBBytes = BN * BK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+// CTA pair (cta_group::2): the pair computes a 256 x 256 tile; each CTA stages its 128 rows
+// of A and one 128-row half of B, and holds its 128 accumulator rows in its own TMEM.
+constexpr uint32_t kPairStageBytes = kTileABytes + kTileBBytes / 2;  // 32 KB
 constexpr int kTmemCols = 2 * BN;  // two accumulator buffers
 // Norm-GEMM workspace layout: a fixed region of arrival counters first, then the per-row
 // partials. The counters sit at the same place for every problem shape, so launches of
@@ -72,6 +75,7 @@ struct Cfg;
 template <>
 struct Cfg<kEpiAct> {
   static constexpr int kStages = 4;
+  static constexpr int kPairStages = 6;
   // 2 halves x 2 staging tiles (128 rows x 32 bf16, 64-byte swizzle) + 128 floats
   static constexpr uint32_t kEpiBytes = 4 * kStgBytes + 512;
   static constexpr int kNumCBuf = 0;
@@ -80,6 +84,7 @@ struct Cfg<kEpiAct> {
 template <>
 struct Cfg<kEpiNorm> {
   static constexpr int kStages = 4;
+  static constexpr int kPairStages = 0;  // no pair variant: the exchange wants 1-CTA tiles
   static constexpr uint32_t kEpiBytes = 4 * kStgBytes + 512;
   static constexpr int kNumCBuf = 0;
   static constexpr int kEpiArrivals = 2 * kEpiThreads;
@@ -92,6 +97,7 @@ struct Cfg<kEpiNorm> {
 template <>
 struct Cfg<kEpiResidual> {
   static constexpr int kStages = 3;
+  static constexpr int kPairStages = 0;  // HBM-bound: the pair buys nothing
   static constexpr int kNumCBuf = 4;
   static constexpr int kLookahead = 2;
   static constexpr bool kXStaged = true;  // bf16 copy staged (64-byte swizzle) + TMA store
@@ -101,6 +107,7 @@ struct Cfg<kEpiResidual> {
 template <>
 struct Cfg<kEpiResidualLongK> {
   static constexpr int kStages = 4;
+  static constexpr int kPairStages = 6;
   static constexpr int kNumCBuf = 2;
   static constexpr int kLookahead = 1;
   static constexpr bool kXStaged = false;  // bf16 copy stored from registers
@@ -108,11 +115,17 @@ struct Cfg<kEpiResidualLongK> {
   static constexpr int kEpiArrivals = kEpiThreads;
 };
 
-template <int KIND>
-constexpr uint32_t smem_bytes() {
-  return 1024 /*alignment slack*/ + Cfg<KIND>::kStages * kStageBytes + Cfg<KIND>::kEpiBytes +
-         256 /*barriers + tmem slot*/;
+template <int KIND, bool PAIR>
+__host__ __device__ constexpr int num_stages() {
+  return PAIR ? Cfg<KIND>::kPairStages : Cfg<KIND>::kStages;
 }
+template <int KIND, bool PAIR>
+constexpr uint32_t smem_bytes() {
+  return 1024 /*alignment slack*/ + num_stages<KIND, PAIR>() * (PAIR ? kPairStageBytes : kStageBytes) +
+         Cfg<KIND>::kEpiBytes + 256 /*barriers + tmem slot*/;
+}
+static_assert(smem_bytes<kEpiAct, true>() <= 232448 && smem_bytes<kEpiResidualLongK, true>() <= 232448,
+              "pair configurations exceed the 227 KB shared-memory limit");
 
 // ---------------------------------------------------------------------------
 // Epilogue helpers
@@ -168,17 +181,22 @@ __device__ __forceinline__ void load_vec64(const float* __restrict__ v, int n0, 
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int KIND>
+template <int KIND, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmC,
                 const __grid_constant__ CUtensorMap tmX, const GemmShape s, const EpiParams p) {
-  constexpr int STAGES = Cfg<KIND>::kStages;
+  constexpr int STAGES = num_stages<KIND, PAIR>();
+  static_assert(STAGES > 0, "no pair variant for this epilogue");
+  constexpr uint32_t SB = PAIR ? kPairStageBytes : kStageBytes;
+  // Accumulator-release arrivals per CTA: one per thread, or (pair) one per warp so that the
+  // peer CTA sends few remote arrivals to the leader.
+  constexpr int kTemptyCount = PAIR ? 2 * (Cfg<KIND>::kEpiArrivals / 32) : Cfg<KIND>::kEpiArrivals;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* stage_base = smem;
-  uint8_t* epi_base = smem + STAGES * kStageBytes;
+  uint8_t* epi_base = smem + STAGES * SB;
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_base + Cfg<KIND>::kEpiBytes);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
@@ -189,6 +207,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Tile schedule. 1-CTA: tile t -> (m_blk, n_blk) = (t / n_blocks, t % n_blocks), CTA b takes
+  // t = b, b + grid, ... Pair: s.tiles counts 256-row pair tiles; pair c = blockIdx / 2 takes
+  // t = c, c + grid/2, ... and CTA rank r of the pair owns 128-row block 2 (t / n_blocks) + r.
+  const int cta_rank = PAIR ? static_cast<int>(cluster_ctarank()) : 0;
+  const int t_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int t_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  auto tile_coords = [&](int t, int& m_blk, int& n_blk) {
+    const int mq = t / s.n_blocks;
+    n_blk = t - mq * s.n_blocks;
+    m_blk = PAIR ? 2 * mq + cta_rank : mq;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -197,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
-      mbar_init(&tempty_bar[i], Cfg<KIND>::kEpiArrivals);
+      mbar_init(&tempty_bar[i], kTemptyCount);
     }
     for (int i = 0; i < 8; ++i) mbar_init(&cload_bar[i], 1);
     fence_mbar_init();
@@ -208,11 +237,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.has_out_map) tma_prefetch_desc(&tmOut);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    cluster_sync_all();  // both CTAs' barriers initialized before any cross-CTA signal
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -221,15 +259,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < s.tiles; tile += gridDim.x) {
-        const int m_blk = tile / s.n_blocks;
-        const int n_blk = tile - m_blk * s.n_blocks;
+      for (int tile = t_first; tile < s.tiles; tile += t_step) {
+        int m_blk, n_blk;
+        tile_coords(tile, m_blk, n_blk);
         for (int kb = 0; kb < s.k_blocks; ++kb) {
-          if (!wait_parity(&empty_bar[stage], phase ^ 1u, kSiteProducerEmpty)) goto producer_done;
-          uint8_t* st = stage_base + stage * kStageBytes;
-          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
-          tma_load_2d(st, &tmA, &full_bar[stage], kb * BK, m_blk * BM);
-          tma_load_2d(st + kTileABytes, &tmB, &full_bar[stage], kb * BK, n_blk * BN);
+          if (!wait_parity<PAIR>(&empty_bar[stage], phase ^ 1u, kSiteProducerEmpty)) goto producer_done;
+          uint8_t* st = stage_base + stage * SB;
+          if constexpr (PAIR) {
+            // Both CTAs' loads complete on the leader's full barrier; only the leader arms it.
+            const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+            if (cta_rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * SB);
+            tma_load_2d_pair(st, &tmA, fb, kb * BK, m_blk * BM);
+            tma_load_2d_pair(st + kTileABytes, &tmB, fb, kb * BK, n_blk * BN + cta_rank * (BN / 2));
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], SB);
+            tma_load_2d(st, &tmA, &full_bar[stage], kb * BK, m_blk * BM);
+            tma_load_2d(st + kTileABytes, &tmB, &full_bar[stage], kb * BK, n_blk * BN);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -238,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: do not leave the CTA while TMA writes into its shared memory are pending.
       for (int i = 0; i < STAGES; ++i) {
-        if (!wait_parity(&empty_bar[stage], phase ^ 1u, kSiteDrain)) break;
+        if (!wait_parity<PAIR>(&empty_bar[stage], phase ^ 1u, kSiteDrain)) break;
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -249,40 +295,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ----------------------------- MMA issuer -------------------------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    // Pair: the leader (rank 0) issues cta_group::2 MMAs over both CTAs' stages and signals
+    // both CTAs' barriers (one commit per barrier); the peer's warp 1 only owns TMEM.
+    if (lane == 0 && cta_rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int tile = blockIdx.x; tile < s.tiles; tile += gridDim.x, ++it) {
+      for (int tile = t_first; tile < s.tiles; tile += t_step, ++it) {
         const int buf = it & 1;
         const uint32_t tphase = (it >> 1) & 1;
-        if (!wait_parity(&tempty_bar[buf], tphase ^ 1u, kSiteMmaTmemEmpty)) break;
+        if (!wait_parity<PAIR>(&tempty_bar[buf], tphase ^ 1u, kSiteMmaTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         bool ok = true;
         for (int kb = 0; kb < s.k_blocks; ++kb) {
-          if (!wait_parity(&full_bar[stage], phase, kSiteMmaFull)) {
+          if (!wait_parity<PAIR>(&full_bar[stage], phase, kSiteMmaFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(stage_base + stage * kStageBytes);
+          const uint32_t a_addr = smem_u32(stage_base + stage * SB);
           const uint64_t a_desc = smem_desc_sw128(a_addr);
           const uint64_t b_desc = smem_desc_sw128(a_addr + kTileABytes);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // Advance 16 bf16 (32 bytes) along K inside the swizzle atom: +2 in addr>>4.
-            mma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (PAIR) {
+              mma_bf16_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            } else {
+              mma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
           }
-          mma_commit(&empty_bar[stage]);
+          if constexpr (PAIR) {
+            mma_commit_pair(smem_u32(&empty_bar[stage]));
+            mma_commit_pair(mapa_shared(smem_u32(&empty_bar[stage]), 1));
+          } else {
+            mma_commit(&empty_bar[stage]);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull_bar[buf]);
+        if constexpr (PAIR) {
+          mma_commit_pair(smem_u32(&tfull_bar[buf]));
+          mma_commit_pair(mapa_shared(smem_u32(&tfull_bar[buf]), 1));
+        } else {
+          mma_commit(&tfull_bar[buf]);
+        }
       }
     }
     __syncwarp();
@@ -299,6 +361,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = wq * 32 + lane;     // accumulator row inside the tile
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const int col_base = half * (BN / 2);
+    // Hand accumulator buffer b back to the MMA issuer (the pair leader's barrier in pair mode).
+    auto release_acc = [&](int b) {
+      tc_fence_before();
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[b]), 0));
+      } else {
+        mbar_arrive(&tempty_bar[b]);
+      }
+    };
 
     if constexpr (KIND == kEpiAct || KIND == kEpiNorm) {
       constexpr int kChunks = (BN / 2) / 32;  // 32-column chunks per half
@@ -322,13 +394,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pending_ctr = nullptr;
       };
-      for (int tile = blockIdx.x; tile < s.tiles && !failed; tile += gridDim.x, ++it) {
-        const int m_blk = tile / s.n_blocks;
-        const int n_blk = tile - m_blk * s.n_blocks;
+      for (int tile = t_first; tile < s.tiles && !failed; tile += t_step, ++it) {
+        int m_blk, n_blk;
+        tile_coords(tile, m_blk, n_blk);
+        const bool rows_any = m_blk * BM < s.M;  // false only for a pair's trailing half
         const int buf = it & 1;
         const uint32_t tphase = (it >> 1) & 1;
         {
-          const bool ok = wait_parity(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
+          const bool ok = wait_parity<PAIR>(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
           if (named_bar_any(3, 2 * kEpiThreads, !ok)) break;
         }
         if (KIND == kEpiNorm) release_pending();
@@ -390,8 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ss = fmaf(f.y, f.y, ss);
             }
           }
-          tc_fence_before();
-          mbar_arrive(&tempty_bar[buf]);
+          release_acc(buf);
 
           const bool do_rope = group < p.rope_groups;
           const float* cb = nullptr;
@@ -499,8 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           if (c == kChunks - 1) {
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[buf]);
+            release_acc(buf);
           }
           if (n0 >= s.N) continue;  // uniform inside the half
           finish_linear(v, n0);
@@ -522,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           named_bar_sync(bar_half, kEpiThreads);
           if (ht == 0) {
-            tma_store_2d(&tmOut, stg_half_ptr + sbuf * kStgBytes, n0, m_blk * BM);
+            if (rows_any) tma_store_2d(&tmOut, stg_half_ptr + sbuf * kStgBytes, n0, m_blk * BM);
             bulk_commit();
           }
           sbuf ^= 1;
@@ -543,16 +614,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr bool XS = Cfg<KIND>::kXStaged;
       uint8_t* cbuf0 = epi_base;
       uint8_t* xbuf0 = epi_base + NB * 16384;
-      const int my_tiles = (blockIdx.x < s.tiles) ? (s.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      const int my_tiles = (t_first < s.tiles) ? (s.tiles - 1 - t_first) / t_step + 1 : 0;
       const int total_chunks = my_tiles * CPT;
       const bool has_x = p.has_x_map;
       // Chunk g -> (tile, column chunk); issue the residual load of chunk g.
       auto issue_load = [&](int g) {
         const int ti = g / CPT;
         const int c = g - ti * CPT;
-        const int tile = blockIdx.x + ti * gridDim.x;
-        const int m_blk = tile / s.n_blocks;
-        const int n_blk = tile - m_blk * s.n_blocks;
+        int m_blk, n_blk;
+        tile_coords(t_first + ti * t_step, m_blk, n_blk);
         const int n0 = n_blk * BN + c * 32;
         uint64_t* bar = &cload_bar[g % NB];
         mbar_arrive_expect_tx(bar, 16384);
@@ -564,13 +634,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;
       bool failed = false;
       for (int ti = 0; ti < my_tiles && !failed; ++ti) {
-        const int tile = blockIdx.x + ti * gridDim.x;
-        const int m_blk = tile / s.n_blocks;
-        const int n_blk = tile - m_blk * s.n_blocks;
+        int m_blk, n_blk;
+        tile_coords(t_first + ti * t_step, m_blk, n_blk);
+        const bool rows_any = m_blk * BM < s.M;  // false only for a pair's trailing half
         const int buf = ti & 1;
         const uint32_t tphase = (ti >> 1) & 1;
         {
-          const bool ok = wait_parity(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
+          const bool ok = wait_parity<PAIR>(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
           if (named_bar_any(2, kEpiThreads, !ok)) break;
         }
         tc_fence_after();
@@ -590,8 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float acc[32];
           tmem_ld32(tmem_base + lane_off + buf * BN + c * 32, acc);
           if (c == CPT - 1) {
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[buf]);
+            release_acc(buf);
           }
           const bool c_ok = wait_parity(&cload_bar[g % NB], (g / NB) & 1, kSiteEpiCLoad);
           const bool col_ok = n0 < s.N;
@@ -677,7 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if (et == 0) {
-            if (col_ok) {
+            if (col_ok && rows_any) {
               tma_store_2d(&tmOut, cbuf0 + (g % NB) * 16384, n0, m_blk * BM);
               if (XS && has_x) tma_store_2d(&tmX, xbuf0 + (g & 1) * kStgBytes, n0, m_blk * BM);
             }
@@ -698,11 +767,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  __syncthreads();
+  tc_fence_before();
+  if constexpr (PAIR) {
+    cluster_sync_all();  // neither CTA leaves while the other may still signal or read it
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    } else {
+      tmem_dealloc(tmem_base, kTmemCols);
+    }
   }
 }
 
@@ -767,45 +845,69 @@ int num_sms() {
   return g_num_sms;
 }
 
-template <int KIND>
+// Whether the tensor-bound variants (bias/GELU, long-K residual) run on CTA pairs.
+int g_cta_pair = 1;
+
+template <int KIND, bool PAIR>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const CUtensorMap& c,
-           const CUtensorMap& x, const GemmShape& s, const EpiParams& p, cudaStream_t stream, bool cooperative,
+           const CUtensorMap& x, const GemmShape& shape, const EpiParams& p, cudaStream_t stream, bool cooperative,
            int max_ctas, int min_grid = 1) {
   static bool attr_set[64] = {};
+  static int pair_slots[64] = {};  // co-resident CTA pairs per device
   int dev = 0;
   cudaGetDevice(&dev);
-  constexpr uint32_t smem = smem_bytes<KIND>();
+  constexpr uint32_t smem = smem_bytes<KIND, PAIR>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = cooperative ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = PAIR ? 2 : 1;
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+    if (PAIR) {
+      int n = 0;
+      cfg.gridDim = dim3(2);
+      e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<KIND, PAIR>, &cfg);
+      if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+      if (n <= 0) return WDIT_ERR_CUDA_BASE + static_cast<int>(cudaErrorInvalidConfiguration);
+      pair_slots[dev & 63] = n;
+    }
     attr_set[dev & 63] = true;
   }
+  GemmShape s = shape;
   int grid = num_sms();
-  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
-  if (max_ctas <= 0 && min_grid > 1 && s.tiles > grid) {
-    // Norm epilogue: a multiple of the group size keeps a group's tiles in one wave (no
-    // waiting on the next wave), and a grid that is not a multiple of the column-tile count
-    // rotates every CTA through normalized and plain tiles (their epilogue costs differ).
-    int g = grid - grid % min_grid;
-    while (g > min_grid && p.norm_groups * min_grid < s.n_blocks && g % s.n_blocks == 0) g -= min_grid;
-    if (g >= min_grid) grid = g;
+  if (PAIR) {
+    s.tiles = ((s.m_blocks + 1) / 2) * s.n_blocks;  // 256-row pair tiles
+    grid = 2 * pair_slots[dev & 63];
+    if (max_ctas > 0 && max_ctas < grid) grid = max_ctas < 2 ? 2 : max_ctas & ~1;
+    if (2 * s.tiles < grid) grid = 2 * s.tiles;
+  } else {
+    if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
+    if (max_ctas <= 0 && min_grid > 1 && s.tiles > grid) {
+      // Norm epilogue: a multiple of the group size keeps a group's tiles in one wave (no
+      // waiting on the next wave), and a grid that is not a multiple of the column-tile count
+      // rotates every CTA through normalized and plain tiles (their epilogue costs differ).
+      int g = grid - grid % min_grid;
+      while (g > min_grid && p.norm_groups * min_grid < s.n_blocks && g % s.n_blocks == 0) g -= min_grid;
+      if (g >= min_grid) grid = g;
+    }
+    if (s.tiles < grid) grid = s.tiles;
   }
-  if (s.tiles < grid) grid = s.tiles;
   if (grid <= 0) return WDIT_OK;
   // The cross-tile exchange of the norm epilogue needs the tiles of one group on distinct,
   // co-resident CTAs: a grid smaller than the group would wait on its own later tile.
   if (grid < min_grid) return WDIT_ERR_ARG;
-  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = cooperative ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<KIND>, a, b, o, c, x, s, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, PAIR>, a, b, o, c, x, s, p);
   return e == cudaSuccess ? WDIT_OK : WDIT_ERR_CUDA_BASE + static_cast<int>(e);
 }
 
@@ -831,11 +933,17 @@ GemmShape make_shape(int M, int N, int K) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-int build_ab(CUtensorMap* ma, CUtensorMap* mb, const void* A, int lda, const void* B, int ldb, int M, int N, int K) {
+// pair: each CTA of a pair loads one 128-row half of the B tile.
+int build_ab(CUtensorMap* ma, CUtensorMap* mb, const void* A, int lda, const void* B, int ldb, int M, int N, int K,
+             bool pair = false) {
   int rc = make_map(ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, K, M, lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  return make_map(mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, K, N, ldb, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_map(mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, K, N, ldb, BK, pair ? BN / 2 : BN,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
 }
+
+// Pairs pay off once there are several 256-row blocks to spread over the GPU.
+bool use_pair(int M) { return g_cta_pair != 0 && M > 2 * BM; }
 
 int ln_fill(LnFold* ln, const float* csum, const float* stats, int stats_tiles, int stats_width, int row_len,
             float eps) {
@@ -862,6 +970,12 @@ extern "C" {
 int wdit_stats_tile_width(void) { return BN; }
 
 int wdit_num_sms(void) { return num_sms(); }
+
+int wdit_set_cta_pair(int enable) {
+  const int prev = g_cta_pair;
+  g_cta_pair = enable != 0 ? 1 : 0;
+  return prev;
+}
 
 int wdit_set_wait_limit_ns(unsigned long long ns) {
   cudaError_t e = cudaMemcpyToSymbol(g_wdit_wait_limit_ns, &ns, sizeof(ns));
@@ -905,11 +1019,15 @@ int wdit_gemm_act(const void* A, int lda, const void* B, int ldb, void* out, int
   p.has_out_map = 1;
   CUtensorMap ma, mb, mo, none;
   memset(&none, 0, sizeof(none));
-  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
+  const bool pair = use_pair(M);
+  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K, pair))) return rc;
   if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  return launch<kEpiAct>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), false,
-                         max_ctas);
+  if (pair)
+    return launch<kEpiAct, true>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
+                                 false, max_ctas);
+  return launch<kEpiAct, false>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
+                                false, max_ctas);
 }
 
 int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const float* C, int ldc, float* out, int ldo,
@@ -948,7 +1066,11 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
   p.ldx = ldx;
   CUtensorMap ma, mb, mo, mc, mx;
   memset(&mx, 0, sizeof(mx));
-  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
+  // Long reductions are tensor-bound (deeper mainloop, CTA pairs), short ones HBM-bound
+  // (deeper residual ring).
+  const bool long_k = K >= 4096;
+  const bool pair = long_k && use_pair(M);
+  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K, pair))) return rc;
   if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, C, N, M, ldc, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -958,12 +1080,11 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
   if (x_bf16_out != nullptr &&
       (rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x_bf16_out, N, M, ldx, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  // Long reductions are tensor-bound (deeper mainloop), short ones HBM-bound (deeper ring).
-  if (K >= 4096)
-    return launch<kEpiResidualLongK>(ma, mb, mo, mc, mx, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
-                                     false, max_ctas);
-  return launch<kEpiResidual>(ma, mb, mo, mc, mx, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), false,
-                              max_ctas);
+  const GemmShape shape = make_shape(M, N, K);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pair) return launch<kEpiResidualLongK, true>(ma, mb, mo, mc, mx, shape, p, st, false, max_ctas);
+  if (long_k) return launch<kEpiResidualLongK, false>(ma, mb, mo, mc, mx, shape, p, st, false, max_ctas);
+  return launch<kEpiResidual, false>(ma, mb, mo, mc, mx, shape, p, st, false, max_ctas);
 }
 
 long long wdit_gemm_norm_workspace_bytes(int M, int N, int norm_groups, int norm_width) {
@@ -1027,7 +1148,7 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
   if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
   if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  return launch<kEpiNorm>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
+  return launch<kEpiNorm, false>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
                           norm_groups > 0, max_ctas, norm_groups > 0 ? norm_width / BN : 1);
 }
 
@@ -1144,7 +1265,7 @@ int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* 
   if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
   if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-  return launch<kEpiNorm>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), true,
+  return launch<kEpiNorm, false>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), true,
                           max_ctas, norm_width / BN);
 }
 

@@ -179,8 +179,10 @@ def main():
     ap.add_argument("--only", type=str, default="")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--pair", type=int, default=1, help="CTA pairs for the tensor-bound GEMMs (1) or not (0)")
     a = ap.parse_args()
     only = set(a.only.split(",")) if a.only else None
+    _pkg()._lib.load().wdit_set_cta_pair(a.pair)
     run(a.m, only, a.iters, not a.no_cublas)
 
 

@@ -71,6 +71,23 @@ def stats_tiles(D: int) -> int:
 # ---------------------------------------------------------------------------
 # Low-level fused GEMMs
 # ---------------------------------------------------------------------------
+class cta_pair:
+    """Context manager selecting whether the tensor-bound GEMMs (``gemm_act``, long-K
+    ``gemm_residual``) run on CTA pairs (256 x 256 tiles, the default) or on single CTAs."""
+
+    def __init__(self, enable: bool):
+        self.enable = bool(enable)
+        self.prev = None
+
+    def __enter__(self):
+        self.prev = _lib.load().wdit_set_cta_pair(1 if self.enable else 0)
+        return self
+
+    def __exit__(self, *exc):
+        _lib.load().wdit_set_cta_pair(self.prev)
+        return False
+
+
 class LnFold:
     """Absorbed LayerNorm: rstd_m * (acc - mu_m * csum[n]); (mu, rstd) from stats partials."""
 

@@ -44,6 +44,11 @@ extern "C" {
 /* Number of SMs of the current device (the persistent grid size). */
 int wdit_num_sms(void);
 
+/* Run the tensor-bound GEMMs (wdit_gemm_act, wdit_gemm_residual with K >= 4096) on CTA pairs
+ * (tcgen05 cta_group::2, 256 x 256 tiles) when M > 256: 1 = on (default), 0 = one CTA per
+ * 128 x 256 tile. Process-wide; returns the previous setting. Results are identical. */
+int wdit_set_cta_pair(int enable);
+
 /* Make `device` current for this library's CUDA runtime in the calling thread (the library
  * links its own runtime; callers keep it equal to their framework's current device). */
 int wdit_set_device(int device);

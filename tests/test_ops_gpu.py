@@ -97,6 +97,44 @@ def test_gemm_residual(pkg, M, N, K, gate, inplace):
         assert got.data_ptr() == c.data_ptr()
 
 
+@pytest.mark.parametrize("M,N,K", [(257, 512, 256), (1000, 64, 4096), (4095, 8960, 1536), (32760, 8960, 1536)])
+def test_gemm_act_cta_pair(pkg, M, N, K):
+    """CTA-pair (256-row tiles, incl. a trailing half past M) vs single-CTA tiles vs fp32."""
+    a = rand((M, K), seed=30)
+    w = rand((N, K), 0.02, seed=31)
+    b = rand((N,), 0.01, seed=32, dtype=torch.float32)
+    with pkg.ops.cta_pair(True):
+        got2 = pkg.ops.gemm_act(a, w, vec=b, act="gelu_tanh")
+    with pkg.ops.cta_pair(False):
+        got1 = pkg.ops.gemm_act(a, w, vec=b, act="gelu_tanh")
+    want = fused_ref.gelu_tanh(a.float() @ w.float().t() + b)
+    assert rel_l2(got2, want) < 5e-3
+    # same K order per output element: at most one bf16 rounding step apart
+    assert rel_l2(got2, got1) < 1e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 1536, 4096), (4095, 1536, 8960), (32760, 1536, 8960)])
+def test_gemm_residual_long_k_cta_pair(pkg, M, N, K):
+    a = rand((M, K), seed=33)
+    w = rand((N, K), 0.02, seed=34)
+    c = rand((M, N), 1.0, seed=35, dtype=torch.float32)
+    bias = rand((N,), 0.01, seed=36, dtype=torch.float32)
+    g = rand((N,), 0.1, seed=37, dtype=torch.float32)
+    outs = []
+    for pair in (True, False):
+        xb = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+        stats = torch.empty((M, (N + 255) // 256, 2), dtype=torch.float32, device=DEV)
+        with pkg.ops.cta_pair(pair):
+            got = pkg.ops.gemm_residual(a, w, c, out=torch.empty_like(c), bias=bias, gate_a=g, x_bf16_out=xb,
+                                        stats_out=stats)
+        assert torch.equal(xb, got.to(torch.bfloat16))
+        assert torch.allclose(stats, fused_ref.ln_stats(got), rtol=1e-4, atol=1e-3)
+        outs.append(got)
+    want = fused_ref.linear_gate_bias_residual(a, w.t(), c, g, bias)
+    assert rel_l2(outs[0], want) < 1e-4
+    assert rel_l2(outs[0], outs[1]) < 1e-6
+
+
 def test_gemm_residual_per_batch_gate(pkg):
     B, L, D, K = 2, 300, 512, 256
     a = rand((B * L, K), seed=20)

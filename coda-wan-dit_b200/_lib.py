@@ -43,7 +43,7 @@ _SIGNATURES = {
     "wdit_set_wait_limit_ns": (c_int, [c_ulonglong]),
     "wdit_read_error": (c_int, [P, I]),
     "wdit_wait_selftest": (c_int, [P, P]),
-    "wdit_gemm_act": (c_int, [P, I, P, I, P, I, I, I, I, P, I, P, P, I, I, F, P, I]),
+    "wdit_gemm_act": (c_int, [P, I, P, I, P, I, I, I, I, P, I, P, P, I, I, F, P, I, I, P, I]),
     "wdit_gemm_residual": (c_int, [P, I, P, I, P, I, P, I, I, I, I, P, P, P, I, I, P, I, P, P, I]),
     "wdit_gemm_norm_workspace_bytes": (c_longlong, [I, I, I, I]),
     "wdit_gemm_norm": (
@@ -61,7 +61,6 @@ _SIGNATURES = {
     "wdit_rmsnorm": (c_int, [P, I, I, I, P, F, P, I, P]),
     "wdit_qk_rms_rope_from_partials": (c_int, [P, I, P, I, I, P, P, P, P, F, P]),
     "wdit_rope_table": (c_int, [P, I, I, I, I, I, P, P, P]),
-    "wdit_block_mean_sq": (c_int, [P, I, I, I, I, P, P]),
     "wdit_ulysses_pack": (c_int, [P, I, I, I, I, I, I, I, P, P]),
     "wdit_seq_gather": (c_int, [P, I, I, I, I, I, P, P]),
     "wdit_seq_scatter": (c_int, [P, c_longlong, c_longlong, I, I, I, I, P, P]),
@@ -123,12 +122,13 @@ _LAUNCHING = {
 launch_counter = {"n": 0}
 
 
-def call(name: str, *args) -> int:
-    """Call a library entry point on the current torch device and raise on failure."""
+def call(name: str, *args, kernels: int = 1) -> int:
+    """Call a library entry point on the current torch device and raise on failure.
+    `kernels`: device kernels the entry point launches (counted in launch_counter)."""
     lib = load()
     _sync_device(lib)
     if name in _LAUNCHING:
-        launch_counter["n"] += 1
+        launch_counter["n"] += kernels
     rc = getattr(lib, name)(*args)
     if isinstance(rc, int) and name not in ("wdit_gemm_norm_workspace_bytes", "wdit_static_scratch_bytes"):
         check(rc, name)

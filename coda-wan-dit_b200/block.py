@@ -10,7 +10,8 @@ Counterpart of coda_wan/run_wan_coda.py:82-205 (CodaFullBlock).
 Per block, on one stream (M = B * L rows):
 
     fold QKV weight      W' = W * (1 + mod1 + e1), csum, vec = (mod0 + e0)^T W + b
-    QKV GEMM             LN absorbed + bias, full-width q/k RMSNorm, 3D RoPE  -> qkv bf16
+    QKV GEMM             LN absorbed + bias -> qkv bf16 + q/k mean-square partials, then the
+                         in-place full-width q/k RMSNorm + 3D RoPE pass
     self-attention       PyTorch SDPA (or the Ulysses all-to-all around it)
     self-O GEMM          x += (y Wo^T + bo) * (mod2 + e2)   -> x fp32, bf16 copy, LN stats
     cross-Q GEMM         norm3 folded statically (gamma into W, beta into vec) + RMSNorm
@@ -181,8 +182,8 @@ class FusedWanBlock(nn.Module):
                              persistent=False)
         self._rope = {}
         if rope_cos is not None and rope_sin is not None:
-            # reference layout [tokens, 64] -> pair-major [64, tokens]
-            self._rope["given"] = (rope_cos.float().t().contiguous(), rope_sin.float().t().contiguous())
+            # the reference's token-major [tokens, 64] tables are the kernel's layout
+            self._rope["given"] = (rope_cos.float().contiguous(), rope_sin.float().contiguous())
 
     # ------------------------------------------------------------------
     def _rope_tables(self, grid, freqs):
@@ -191,7 +192,7 @@ class FusedWanBlock(nn.Module):
         key = (tuple(grid), freqs.data_ptr())
         tab = self._rope.get(key)
         if tab is None:
-            tab = ops.build_rope_table_pair_major(grid, freqs)
+            tab = ops.build_wan_rope_table(grid, freqs)
             self._rope = {key: tab}
         return tab
 

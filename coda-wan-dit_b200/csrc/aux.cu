@@ -7,7 +7,9 @@
 //                        csum[n] = sum_k W'[n,k], vec[n] = sum_k shift[k] W[n,k] + b[n].
 //   layernorm_mod_kernel reference op coda_wan/wan_coda_kernels.py:35-81.
 //   rmsnorm_kernel       reference op coda_wan/wan_coda_kernels.py:371-411.
-//   qk_rms_rope_kernel   reference op coda_wan/wan_coda_kernels.py:233-352.
+//   rms_rope_apply_kernel full-width RMSNorm (+ RoPE) from mean-square partials, in place:
+//                        the second half of every norm GEMM and the reference op
+//                        coda_wan/wan_coda_kernels.py:233-352.
 //   rope_table_kernel    reference op coda_wan/wan_coda_kernels.py:414-430.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -219,41 +221,102 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
 }
 
 // ---------------------------------------------------------------------------
-// One warp per (row, half): half 0 = q, half 1 = k, each D wide, normalized in place.
-__global__ void __launch_bounds__(256)
-    qk_rms_rope_kernel(__nv_bfloat16* __restrict__ qk, int ldqk, const float* __restrict__ partial, int M, int D,
-                       const float* __restrict__ wq, const float* __restrict__ wk, const float* __restrict__ cs,
-                       const float* __restrict__ sn, float eps) {
-  const int item = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+// One warp per row: full-width RMSNorm of each of the row's `groups` column groups (`width`
+// columns each) from per-128-column mean-square partials, then (rope groups) the 3D RoPE
+// rotation, in place. Lane l handles the 16-byte vectors at columns l*8 + 256*j; with
+// 128-column heads those always hold the rotation pairs 4*(l%16) .. 4*(l%16)+3, so each lane
+// fetches its 4 (cos, sin) once per row (two 16-byte loads from the token-major tables, shared
+// by q and k). The first kApplyVec vectors of the row are requested before the partials are
+// reduced, so one memory latency covers both.
+// Arithmetic of coda_wan/wan_coda_kernels.py:233-352 (_qk_rms_rope_kernel): mean square =
+// mean of the block partials, y = bf16(bf16(x * rsqrt(ms + eps)) * w), then the rotation
+// (y_e cos - y_o sin, y_e sin + y_o cos) in fp32 and one bf16 rounding.
+constexpr int kApplyVec = 12;       // 16-byte vectors per lane in flight (2 x 1536 columns)
+constexpr int kApplyRowsPerBlock = 4;
+
+__device__ __forceinline__ uint4 ld_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__global__ void __launch_bounds__(32 * kApplyRowsPerBlock)
+    rms_rope_apply_kernel(__nv_bfloat16* __restrict__ x, int ldx, int M, const float* __restrict__ part,
+                          int part_ld, int groups, int width, const float* __restrict__ w0,
+                          const float* __restrict__ w1, float eps, int rope_groups, const float* __restrict__ cs,
+                          const float* __restrict__ sn, int rope_ld, int rows_per_batch, int token_offset) {
+  const int row = blockIdx.x * kApplyRowsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const int row = item >> 1;
-  const int half = item & 1;
   if (row >= M) return;
-  const int parts = D / 128;
-  float ms = 0.f;
-  for (int j = lane; j < parts; j += 32) ms += partial[static_cast<size_t>(row) * 2 * parts + half * parts + j];
-  ms = warp_sum(ms) / static_cast<float>(parts);
-  const float rstd = rsqrtf(ms + eps);
-  const float* w = half == 0 ? wq : wk;
-  __nv_bfloat16* base = qk + static_cast<size_t>(row) * ldqk + half * D;
-  for (int c = lane * 8; c < D; c += 256) {
-    float v[8];
-    load8(base, true, c, v);
+  const int total = groups * width;
+  __nv_bfloat16* base = x + static_cast<size_t>(row) * ldx;
+  uint4 raw[kApplyVec];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float y = __bfloat162float(__float2bfloat16_rn(v[i] * rstd));
-      v[i] = __bfloat162float(__float2bfloat16_rn(y * w[c + i]));
+  for (int u = 0; u < kApplyVec; ++u) {
+    const int c = lane * 8 + 256 * u;
+    if (c < total) raw[u] = ld_v4(base + c);
+  }
+  const int parts = width / 128;
+  const float* pr = part + static_cast<size_t>(row) * part_ld;
+  float ms0 = 0.f, ms1 = 0.f;
+  for (int j = lane; j < parts; j += 32) {
+    ms0 += pr[j];
+    if (groups > 1) ms1 += pr[parts + j];
+  }
+  float4 c4 = make_float4(1.f, 1.f, 1.f, 1.f), s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (rope_groups > 0) {
+    const int b = row / rows_per_batch;
+    const size_t tok = static_cast<size_t>(row - b * rows_per_batch + token_offset);
+    c4 = __ldg(reinterpret_cast<const float4*>(cs + tok * rope_ld) + (lane & 15));
+    s4 = __ldg(reinterpret_cast<const float4*>(sn + tok * rope_ld) + (lane & 15));
+  }
+  const float rstd0 = rsqrtf(warp_sum(ms0) / static_cast<float>(parts) + eps);
+  const float rstd1 = rsqrtf(warp_sum(ms1) / static_cast<float>(parts) + eps);
+  const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+  const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
+  for (int c0 = 0; c0 < total; c0 += 256 * kApplyVec) {
+    if (c0 > 0) {
+#pragma unroll
+      for (int u = 0; u < kApplyVec; ++u) {
+        const int c = c0 + lane * 8 + 256 * u;
+        if (c < total) raw[u] = ld_v4(base + c);
+      }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int pair = ((c + 2 * i) & 127) >> 1;
-      const float cc = cs[static_cast<size_t>(row) * 64 + pair];
-      const float ss = sn[static_cast<size_t>(row) * 64 + pair];
-      const float e = v[2 * i], o = v[2 * i + 1];
-      v[2 * i] = e * cc - o * ss;
-      v[2 * i + 1] = e * ss + o * cc;
+    for (int u = 0; u < kApplyVec; ++u) {
+      const int c = c0 + lane * 8 + 256 * u;
+      if (c >= total) break;
+      const int g = c >= width ? 1 : 0;
+      const int cg = c - g * width;
+      const float* w = g == 0 ? w0 : w1;
+      const float rstd = g == 0 ? rstd0 : rstd1;
+      const float4 wa = __ldg(reinterpret_cast<const float4*>(w + cg));
+      const float4 wb = __ldg(reinterpret_cast<const float4*>(w + cg + 4));
+      const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+      const uint32_t rw[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(rw[i] << 16);
+        v[2 * i + 1] = __uint_as_float(rw[i] & 0xFFFF0000u);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float y = __bfloat162float(__float2bfloat16_rn(v[i] * rstd));
+        v[i] = __bfloat162float(__float2bfloat16_rn(y * wv[i]));
+      }
+      if (g < rope_groups) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float e = v[2 * i], o = v[2 * i + 1];
+          v[2 * i] = e * cc[i] - o * ss[i];
+          v[2 * i + 1] = e * ss[i] + o * cc[i];
+        }
+      }
+      store8_bf16(base, c, v);
     }
-    store8_bf16(base, c, v);
   }
 }
 
@@ -287,6 +350,26 @@ inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) ==
 inline unsigned row_blocks(int rows) { return static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock); }
 
 }  // namespace
+
+int launch_rms_rope_apply(void* x, int ldx, int M, const float* part, int part_ld, int groups, int width,
+                          const float* w0, const float* w1, float eps, int rope_groups, const float* rope_cos,
+                          const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream) {
+  if (x == nullptr || part == nullptr || w0 == nullptr || (groups > 1 && w1 == nullptr)) return WDIT_ERR_ARG;
+  if (M <= 0 || groups < 1 || groups > 2 || width <= 0 || width % 128 != 0 || ldx < groups * width) return WDIT_ERR_SHAPE;
+  if (part_ld < groups * (width / 128)) return WDIT_ERR_SHAPE;
+  if (!a16(x) || ldx % 8 != 0 || !a16(w0) || (w1 && !a16(w1))) return WDIT_ERR_ALIGN;
+  if (rope_groups > 0) {
+    if (rope_cos == nullptr || rope_sin == nullptr || rows_per_batch <= 0 || token_offset < 0) return WDIT_ERR_ARG;
+    if (rope_ld < 64) return WDIT_ERR_SHAPE;
+    if (!a16(rope_cos) || !a16(rope_sin) || rope_ld % 4 != 0) return WDIT_ERR_ALIGN;
+  }
+  const unsigned blocks = static_cast<unsigned>((M + kApplyRowsPerBlock - 1) / kApplyRowsPerBlock);
+  rms_rope_apply_kernel<<<blocks, 32 * kApplyRowsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<__nv_bfloat16*>(x), ldx, M, part, part_ld, groups, width, w0, w1, eps, rope_groups, rope_cos,
+      rope_sin, rope_ld, rows_per_batch, token_offset);
+  return launch_status();
+}
+
 }  // namespace wdit
 
 using namespace wdit;
@@ -345,10 +428,10 @@ int wdit_qk_rms_rope_from_partials(void* qk, int ldqk, const float* partial, int
       sin_tab == nullptr)
     return WDIT_ERR_ARG;
   if (M <= 0 || D <= 0 || D % 128 != 0 || ldqk < 2 * D) return WDIT_ERR_SHAPE;
-  if (!a16(qk) || ldqk % 8 != 0) return WDIT_ERR_ALIGN;
-  qk_rms_rope_kernel<<<row_blocks(2 * M), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<__nv_bfloat16*>(qk), ldqk, partial, M, D, wq, wk, cos_tab, sin_tab, eps);
-  return launch_status();
+  // The reference's partials [M, 2 * D/128] (q blocks, then k blocks) and [M, 64] tables
+  // indexed by row are this pass's layout with two rope groups.
+  return launch_rms_rope_apply(qk, ldqk, M, partial, 2 * (D / 128), 2, D, wq, wk, eps, 2, cos_tab, sin_tab, 64, M, 0,
+                               stream);
 }
 
 int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, int pair_major, float* cos_out,

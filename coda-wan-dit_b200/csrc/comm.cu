@@ -109,25 +109,6 @@ __global__ void ulysses_unpack_kernel(const uint4* __restrict__ recv, int B, int
       recv[((static_cast<long long>(d) * U + j) * Lp + t) * hdv + v];
 }
 
-__global__ void block_mean_sq_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M, int N, int block,
-                                     float* __restrict__ out) {
-  // One warp per (row, block) pair.
-  const long long item = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int nb = N / block;
-  if (item >= static_cast<long long>(M) * nb) return;
-  const int row = static_cast<int>(item / nb);
-  const int blk = static_cast<int>(item - static_cast<long long>(row) * nb);
-  float s = 0.f;
-  for (int c = lane; c < block; c += 32) {
-    const float v = __bfloat162float(x[static_cast<long long>(row) * ldx + blk * block + c]);
-    s = fmaf(v, v, s);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) out[item] = s / static_cast<float>(block);
-}
-
 }  // namespace
 }  // namespace wdit
 
@@ -181,15 +162,6 @@ int wdit_ulysses_unpack(const void* recv, int B, int Lp, int H, int hd, int P, v
   const long long total = static_cast<long long>(B) * Lp * H * (hd / 8);
   ulysses_unpack_kernel<<<blocks_for(total), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(recv), B, Lp, H, hd / 8, P, static_cast<uint4*>(dst), ld / 8);
-  return launch_status();
-}
-
-int wdit_block_mean_sq(const void* x, int ldx, int M, int N, int block, float* out, void* stream) {
-  if (x == nullptr || out == nullptr) return WDIT_ERR_ARG;
-  if (M <= 0 || N <= 0 || block <= 0 || N % block != 0 || ldx < N) return WDIT_ERR_SHAPE;
-  const long long items = static_cast<long long>(M) * (N / block);
-  block_mean_sq_kernel<<<static_cast<unsigned>((items + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, M, N, block, out);
   return launch_status();
 }
 

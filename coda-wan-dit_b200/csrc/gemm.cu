@@ -3,29 +3,32 @@
 //   D[M, N] = A[M, K] . B[N, K]^T      A, B bf16 K-major (B = nn.Linear.weight layout),
 //                                       fp32 accumulation in TMEM.
 //
-// CTA = 6 warps, one CTA per SM, grid = min(#SMs, #tiles), static tile order
+// CTA = 10 warps, one CTA per SM, grid = the co-resident CTA count, static tile order
 // tile -> (m_blk = tile / n_blocks, n_blk = tile % n_blocks):
 //   warp 0     TMA producer: A (128x64) and B (256x64) tiles, 128-byte swizzle,
 //              STAGES-deep shared-memory ring (full/empty mbarriers).
 //   warp 1     TMEM allocator (512 columns = two 128x256 fp32 accumulators) and
 //              single-thread tcgen05.mma issuer (M=128, N=256, K=16 per instruction).
-//   warps 2-5  epilogue: tcgen05.ld (thread = one accumulator row), fused math,
-//              swizzled shared-memory staging, TMA stores.
-// The accumulator is double buffered, so the epilogue of tile i overlaps the
-// mainloop of tile i+1.
+//   warps 2-9  epilogue: tcgen05.ld (thread = one accumulator row; warps 2-5 take columns
+//              0-127 of the tile, warps 6-9 columns 128-255), fused math, swizzled
+//              shared-memory staging, TMA stores. The residual epilogues use warps 2-5.
+// The accumulator is double buffered, so the epilogue of tile i overlaps the mainloop of
+// tile i+1.
+//
+// CTA pairs (PAIR = true, cluster of 2): the tensor-bound variants run 256 x 256 tiles with
+// tcgen05 cta_group::2: each CTA loads its 128 rows of A and one 128-row half of B, the even
+// CTA issues M=256 MMAs over both CTAs' shared memory, and each CTA's epilogue drains its
+// own 128 accumulator rows. Half the B traffic per CTA, same epilogue.
 //
 // Epilogue families (one template instance each):
-//   kEpiAct       out_bf16 = act( LN(acc) + vec )          FFN1 (tanh-GELU), plain bias GEMMs
-//   kEpiResidual  out_f32  = C + (acc + bias) * gate        self-O / FFN2 (gate), cross-O (no gate)
-//                 and optionally a bf16 copy of out plus per-row (mean, M2) partials
-//                 of out over each 256-column tile (the next LayerNorm's statistics).
-//   kEpiNorm      out_bf16 = RoPE( RMSNorm_fullwidth( LN(acc) + vec ) )   QKV, cross-Q, cross-KV
-//                 The full-width RMSNorm needs the sum of squares over D = 1536 (or 5120)
-//                 columns, i.e. over D/256 tiles owned by different CTAs; each tile
-//                 publishes its per-row partial to a global scratch slot and a per
-//                 (row block, group) arrival counter, waits (bounded) for the group, then
-//                 normalizes straight out of TMEM. This kernel is launched cooperatively so
-//                 all CTAs are co-resident (the wait cannot deadlock).
+//   kEpiAct            out_bf16 = act( LN(acc) + vec )      FFN1 (tanh-GELU), QKV, cross-Q,
+//                      cross-KV, text MLP, head; optionally the per-row mean square of the
+//                      bf16 output over each 128-column block (RMSNorm partials, consumed by
+//                      the in-place RMSNorm / RoPE pass in aux.cu).
+//   kEpiResidual       out_f32 = C + (acc + bias) * gate    self-O (gate), cross-O (no gate),
+//   kEpiResidualLongK  (short / long K)                     FFN2 (gate)
+//                      and optionally a bf16 copy of out plus per-row (mean, M2) partials
+//                      of out over each 256-column tile (the next LayerNorm's statistics).
 //
 // LN(acc) is the adaLN LayerNorm absorbed into the GEMM (the modulation scale is folded
 // into the weight each step):  LN(acc) = rstd * (acc - mu * csum[n]),
@@ -33,10 +36,9 @@
 // epilogue (Chan's parallel variance merge), and the shift term added through `vec`.
 //
 // Reference counterparts (Owen718/CODA-Wan-DiT):
-//   kEpiAct       coda_wan/wan_coda_kernels.py:84-152   (EVTGELUBias, linear_bias_gelu_fixed)
-//   kEpiResidual  coda_wan/wan_gate_residual_coda.py:75-135, 138-161, 192-242
-//   kEpiNorm      coda_wan/wan_coda_kernels.py:155-352 (Q+K GEMM with mean-square partials +
-//                 _qk_rms_rope_kernel) and :371-411 (_rmsnorm_kernel)
+//   kEpiAct            coda_wan/wan_coda_kernels.py:84-152 (EVTGELUBias, linear_bias_gelu_fixed)
+//                      and :155-230 (Q+K GEMM with mean-square partials)
+//   kEpiResidual*      coda_wan/wan_gate_residual_coda.py:75-135, 138-161, 192-242
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -55,7 +57,8 @@ constexpr int BN = 256;
 constexpr int BK = 64;
 constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kEpiThreads = 128;  // one column half (4 warps)
-constexpr uint32_t kStgBytes = 8192;  // 128 rows x 32 bf16 output staging tile
+constexpr uint32_t kStgBytes = 8192;       // 128 rows x 32 bf16 output staging tile
+constexpr uint32_t kWarpStgBytes = 2048;   // 32 rows x 32 bf16: one warp's staging buffer
 constexpr uint32_t kTileABytes = BM * BK * 2;  // 16 KB
 constexpr uint32_t kTileBBytes = BN * BK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
@@ -63,12 +66,7 @@ constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 // of A and one 128-row half of B, and holds its 128 accumulator rows in its own TMEM.
 constexpr uint32_t kPairStageBytes = kTileABytes + kTileBBytes / 2;  // 32 KB
 constexpr int kTmemCols = 2 * BN;  // two accumulator buffers
-// Norm-GEMM workspace layout: a fixed region of arrival counters first, then the per-row
-// partials. The counters sit at the same place for every problem shape, so launches of
-// different shapes can share one workspace (partials never overwrite counters).
-constexpr long long kCounterRegionBytes = 64 * 1024;
-
-enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiNorm = 2, kEpiResidualLongK = 3 };
+enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiResidualLongK = 3 };
 
 template <int KIND>
 struct Cfg;
@@ -76,16 +74,8 @@ template <>
 struct Cfg<kEpiAct> {
   static constexpr int kStages = 4;
   static constexpr int kPairStages = 6;
-  // 2 halves x 2 staging tiles (128 rows x 32 bf16, 64-byte swizzle) + 128 floats
-  static constexpr uint32_t kEpiBytes = 4 * kStgBytes + 512;
-  static constexpr int kNumCBuf = 0;
-  static constexpr int kEpiArrivals = 2 * kEpiThreads;
-};
-template <>
-struct Cfg<kEpiNorm> {
-  static constexpr int kStages = 4;
-  static constexpr int kPairStages = 0;  // no pair variant: the exchange wants 1-CTA tiles
-  static constexpr uint32_t kEpiBytes = 4 * kStgBytes + 512;
+  // 8 warps x 2 staging buffers (32 rows x 32 bf16, 64-byte swizzle)
+  static constexpr uint32_t kEpiBytes = 8 * 2 * kWarpStgBytes;
   static constexpr int kNumCBuf = 0;
   static constexpr int kEpiArrivals = 2 * kEpiThreads;
 };
@@ -130,52 +120,44 @@ static_assert(smem_bytes<kEpiAct, true>() <= 232448 && smem_bytes<kEpiResidualLo
 // ---------------------------------------------------------------------------
 // Epilogue helpers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float gelu_tanh(float x) {
-  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))); constants as in
-  // coda_wan/wan_coda_kernels.py:100-101.
-  const float z = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanh_approx(z));
+// tanh-GELU of two columns: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), constants as in
+// coda_wan/wan_coda_kernels.py:100-101, factored as z = x (k + k c x^2), out = h + h tanh(z)
+// with h = x / 2, in packed f32x2 arithmetic.
+__device__ __forceinline__ void gelu_tanh2(float& a, float& b) {
+  constexpr float kK = 0.7978845608028654f;
+  constexpr float kKC = 0.7978845608028654f * 0.044715f;
+  const uint64_t x = f2_pack(a, b);
+  const uint64_t z = fmul2(x, ffma2(fmul2(x, x), f2_pack(kKC, kKC), f2_pack(kK, kK)));
+  float z0, z1;
+  f2_unpack(z, z0, z1);
+  const uint64_t h = fmul2(x, f2_pack(0.5f, 0.5f));
+  f2_unpack(ffma2(h, f2_pack(tanh_approx(z0), tanh_approx(z1)), h), a, b);
 }
 
-// Merge per-tile (mean, M2) partials of one row into (mu, rstd).
+// Merge per-tile (mean, M2) partials of one row into (mu, rstd). The partials are fetched
+// four at a time so their load latencies overlap.
 __device__ __forceinline__ void ln_row_stats(const LnFold& ln, int row, float& mu, float& rstd) {
-  const float* st = ln.stats + static_cast<size_t>(row) * ln.stats_tiles * 2;
+  const float2* st = reinterpret_cast<const float2*>(ln.stats) + static_cast<size_t>(row) * ln.stats_tiles;
   float n = 0.f, mean = 0.f, m2 = 0.f;
-  for (int t = 0; t < ln.stats_tiles; ++t) {
-    const float2 pm = *reinterpret_cast<const float2*>(st + 2 * t);
-    const int rem = ln.row_len - t * ln.stats_width;
-    const float nt = static_cast<float>(rem < ln.stats_width ? rem : ln.stats_width);
-    const float tot = n + nt;
-    const float delta = pm.x - mean;
-    mean += delta * (nt / tot);
-    m2 += pm.y + delta * delta * (n * nt / tot);
-    n = tot;
+  for (int t0 = 0; t0 < ln.stats_tiles; t0 += 4) {
+    float2 pm[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) pm[u] = t0 + u < ln.stats_tiles ? st[t0 + u] : make_float2(0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + u;
+      if (t >= ln.stats_tiles) break;
+      const int rem = ln.row_len - t * ln.stats_width;
+      const float nt = static_cast<float>(rem < ln.stats_width ? rem : ln.stats_width);
+      const float tot = n + nt;
+      const float delta = pm[u].x - mean;
+      mean += delta * (nt / tot);
+      m2 += pm[u].y + delta * delta * (n * nt / tot);
+      n = tot;
+    }
   }
   mu = mean;
   rstd = rsqrtf(m2 / static_cast<float>(ln.row_len) + ln.eps);
-}
-
-// Write 64 bf16 values (32 packed words) of row r into a 128-byte-swizzled staging tile.
-__device__ __forceinline__ void stage_row_sw128(uint32_t tile_addr, int r, const uint32_t (&w)[32]) {
-  const uint32_t row_addr = tile_addr + r * 128;
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const uint32_t a = row_addr + ((q ^ (r & 7)) << 4);
-    st_shared_v4(a, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-  }
-}
-
-// Load 64 consecutive fp32 values of a per-column vector (broadcast across the warp).
-__device__ __forceinline__ void load_vec64(const float* __restrict__ v, int n0, float (&out)[64]) {
-  const float4* p = reinterpret_cast<const float4*>(v + n0);
-#pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    const float4 t = __ldg(p + q);
-    out[4 * q] = t.x;
-    out[4 * q + 1] = t.y;
-    out[4 * q + 2] = t.z;
-    out[4 * q + 3] = t.w;
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -372,64 +354,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
 
-    if constexpr (KIND == kEpiAct || KIND == kEpiNorm) {
+    if constexpr (KIND == kEpiAct) {
       constexpr int kChunks = (BN / 2) / 32;  // 32-column chunks per half
-      const uint32_t stg_half = smem_u32(epi_base) + half * 2 * kStgBytes;
-      uint8_t* stg_half_ptr = epi_base + half * 2 * kStgBytes;
-      float* ss_smem = reinterpret_cast<float*>(epi_base + 4 * kStgBytes);
-      const uint32_t bar_half = 1 + half;
-      const int tiles_per_group = KIND == kEpiNorm ? p.norm_width / BN : 1;
-      const int part_cols = KIND == kEpiNorm ? p.norm_groups * tiles_per_group : 1;
+      // Per-warp staging: two 32-row x 32-column bf16 buffers (64-byte swizzle) per warp, each
+      // stored by the warp's own TMA store, so the warps of a half never wait on each other.
+      uint8_t* stg_warp_ptr = epi_base + ew * 2 * kWarpStgBytes;
+      const uint32_t stg_warp = smem_u32(stg_warp_ptr);
+      const bool use_ln = p.ln.csum != nullptr;
       int sbuf = 0;
       int it = 0;
-      bool failed = false;
-      // Counter of the previous tile's group, released (second-round arrival) only once all
-      // eight warps have passed the next tile-start barrier, i.e. have read its partials.
-      unsigned int* pending_ctr = nullptr;
-      const unsigned int pub_target = 4u * tiles_per_group;  // publishing warps per group
-      auto release_pending = [&]() {
-        if (pending_ctr != nullptr && warp == 2 && lane == 0) {
-          const unsigned int old = atom_add_acq_rel(pending_ctr, 1u);
-          if (old == pub_target + tiles_per_group - 1u) atomicExch(pending_ctr, 0u);
-        }
-        pending_ctr = nullptr;
-      };
-      for (int tile = t_first; tile < s.tiles && !failed; tile += t_step, ++it) {
+      for (int tile = t_first; tile < s.tiles; tile += t_step, ++it) {
         int m_blk, n_blk;
         tile_coords(tile, m_blk, n_blk);
-        const bool rows_any = m_blk * BM < s.M;  // false only for a pair's trailing half
+        const int warp_row0 = m_blk * BM + wq * 32;
+        const bool rows_any = warp_row0 < s.M;  // this warp's 32 rows hold data
         const int buf = it & 1;
         const uint32_t tphase = (it >> 1) & 1;
+        const int row = m_blk * BM + r;
+        const bool row_ok = row < s.M;
+        const int nh = n_blk * BN + col_base;  // first column of this half
+        // What does not need the accumulator happens before waiting for it: the row's
+        // LayerNorm statistics and an L1 prefetch of the half's per-column vectors.
+        float mu = 0.f, rstd = 1.f;
+        if (use_ln && row_ok) ln_row_stats(p.ln, row, mu, rstd);
+        if (lane < 4 && nh + lane * 32 < s.N) {
+          if (use_ln) prefetch_l1(p.ln.csum + nh + lane * 32);
+          if (p.vec != nullptr) prefetch_l1(p.vec + nh + lane * 32);
+        }
+        const float nmr = -mu * rstd;
         {
           const bool ok = wait_parity<PAIR>(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
           if (named_bar_any(3, 2 * kEpiThreads, !ok)) break;
         }
-        if (KIND == kEpiNorm) release_pending();
         tc_fence_after();
-        const int row = m_blk * BM + r;
-        const bool row_ok = row < s.M;
-        float mu = 0.f, rstd = 1.f;
-        const bool use_ln = p.ln.csum != nullptr;
-        if (use_ln && row_ok) ln_row_stats(p.ln, row, mu, rstd);
         const uint32_t tbase = tmem_base + lane_off + buf * BN + col_base;
-        const int group = KIND == kEpiNorm ? (n_blk * BN) / p.norm_width : 0;
-        const bool normed = KIND == kEpiNorm && group < p.norm_groups;
-        float rms = 1.f;
-
-        // acc -> LN(acc) + vec for one 32-column chunk starting at column n0.
-        auto finish_linear = [&](float* v, int n0) {
+        // RMSNorm partials: this half's 128 columns form one partial block.
+        const bool ss_on = p.ss_part != nullptr && nh < p.ss_cols;
+        uint64_t ss2 = f2_pack(0.f, 0.f);
+#pragma unroll 1
+        for (int c = 0; c < kChunks; ++c) {
+          const int n0 = nh + c * 32;
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          if (c == kChunks - 1) release_acc(buf);
+          if (n0 >= s.N) continue;  // uniform inside the half
+          // acc -> rstd * (acc - mu * csum) + vec  (= fma(acc, rstd, fma(-mu rstd, csum, vec))),
+          // two columns per packed instruction
           if (use_ln) {
             const float4* cp = reinterpret_cast<const float4*>(p.ln.csum + n0);
+            const float4* bp = reinterpret_cast<const float4*>(p.vec + n0);
+            const uint64_t rs2 = f2_pack(rstd, rstd);
+            const uint64_t nm2 = f2_pack(nmr, nmr);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
               const float4 c4 = __ldg(cp + q);
-              v[4 * q] = rstd * fmaf(-mu, c4.x, v[4 * q]);
-              v[4 * q + 1] = rstd * fmaf(-mu, c4.y, v[4 * q + 1]);
-              v[4 * q + 2] = rstd * fmaf(-mu, c4.z, v[4 * q + 2]);
-              v[4 * q + 3] = rstd * fmaf(-mu, c4.w, v[4 * q + 3]);
+              float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (p.vec != nullptr) b4 = __ldg(bp + q);
+              const uint64_t t0 = ffma2(nm2, f2_pack(c4.x, c4.y), f2_pack(b4.x, b4.y));
+              const uint64_t t1 = ffma2(nm2, f2_pack(c4.z, c4.w), f2_pack(b4.z, b4.w));
+              f2_unpack(ffma2(f2_pack(v[4 * q], v[4 * q + 1]), rs2, t0), v[4 * q], v[4 * q + 1]);
+              f2_unpack(ffma2(f2_pack(v[4 * q + 2], v[4 * q + 3]), rs2, t1), v[4 * q + 2], v[4 * q + 3]);
             }
-          }
-          if (p.vec != nullptr) {
+          } else if (p.vec != nullptr) {
             const float4* bp = reinterpret_cast<const float4*>(p.vec + n0);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
@@ -440,170 +426,45 @@ __global__ void __launch_bounds__(kThreads, 1)
               v[4 * q + 3] += b4.w;
             }
           }
-        };
-
-        if (normed) {
-          // Pass 1 (unrolled): acc -> LN + vec -> bf16 projection, kept packed in registers,
-          // and this thread's share of the row sum of squares (WanRMSNorm normalizes the
-          // bf16 Linear output). The accumulator is released right after, so the MMA of the
-          // next tile overlaps the exchange and pass 2.
-          uint32_t pk[kChunks][16];
-          float ss = 0.f;
+          if (p.act == 1) {
 #pragma unroll
-          for (int c = 0; c < kChunks; ++c) {
-            const int n0 = n_blk * BN + col_base + c * 32;
-            float v[32];
-            tmem_ld32(tbase + c * 32, v);
-            finish_linear(v, n0);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              pk[c][j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-              const float2 f = unpack_bf16x2(pk[c][j]);
-              ss = fmaf(f.x, f.x, ss);
-              ss = fmaf(f.y, f.y, ss);
-            }
-          }
-          release_acc(buf);
-
-          const bool do_rope = group < p.rope_groups;
-          const float* cb = nullptr;
-          const float* sb = nullptr;
-          float cs_cur[16], sn_cur[16];
-          if (do_rope) {
-            // Pair-major tables: a warp's 32 consecutive tokens read one 128-byte line per
-            // pair. Chunk 0's entries are requested now and land during the exchange.
-            const int rr = row_ok ? row : s.M - 1;
-            const int b = rr / p.rows_per_batch;
-            const int tok = rr - b * p.rows_per_batch + p.token_offset;
-            const int pair0 = ((n_blk * BN + col_base - group * p.norm_width) & 127) >> 1;
-            cb = p.rope_cos + static_cast<size_t>(pair0) * p.rope_ld + tok;
-            sb = p.rope_sin + static_cast<size_t>(pair0) * p.rope_ld + tok;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              cs_cur[i] = __ldg(cb + static_cast<size_t>(i) * p.rope_ld);
-              sn_cur[i] = __ldg(sb + static_cast<size_t>(i) * p.rope_ld);
-            }
-          }
-
-          if (half == 1) ss_smem[r] = ss;
-          named_bar_sync(3, 2 * kEpiThreads);
-          unsigned int* ctr = p.counters + m_blk * p.norm_groups + group;
-          if (half == 0) {
-            // Publish: partial stores, warp barrier, then one release-increment per warp.
-            ss += ss_smem[r];
-            if (row_ok) p.part[static_cast<size_t>(row) * part_cols + n_blk] = ss;
-            __syncwarp();
-            if (lane == 0) red_release_add(ctr, 1u);
-          }
-          // Wait (one lane per warp, acquire) until every tile of the group has published.
-          bool fail_local = false;
-          if (lane == 0 && ld_acquire_gpu(ctr) < pub_target) {
-            const uint64_t t0 = globaltimer_ns();
-            const uint64_t limit = g_wdit_wait_limit_ns;
-            while (ld_acquire_gpu(ctr) < pub_target) {
-              if (globaltimer_ns() - t0 > limit) {
-                report_error(kErrTimeout, kSiteExchange, static_cast<unsigned int>(tile));
-                fail_local = true;
-                break;
-              }
-              __nanosleep(20);
-            }
-          }
-          failed = named_bar_any(3, 2 * kEpiThreads, fail_local);
-          if (failed) break;
-          float tot = 0.f;
-          if (row_ok) {
-            const float* pr = p.part + static_cast<size_t>(row) * part_cols + group * tiles_per_group;
-            for (int t = 0; t < tiles_per_group; ++t) tot += ld_cg_f32(pr + t);
-          }
-          rms = rsqrtf(tot / static_cast<float>(p.norm_width) + p.norm_eps);
-          pending_ctr = ctr;
-
-          // Pass 2 from registers: WanRMSNorm (bf16(bf16(x * rstd) * w)), RoPE, bf16 store of
-          // the row's 64 contiguous bytes per chunk (no inter-warp synchronization).
-          const float* wn = group == 0 ? p.norm_w[0] : p.norm_w[1];
-#pragma unroll
-          for (int c = 0; c < kChunks; ++c) {
-            const int n0 = n_blk * BN + col_base + c * 32;
-            if (do_rope && c > 0) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                cs_cur[i] = __ldg(cb + static_cast<size_t>(16 * c + i) * p.rope_ld);
-                sn_cur[i] = __ldg(sb + static_cast<size_t>(16 * c + i) * p.rope_ld);
-              }
-            }
-            float v[32];
-            const float4* wp = reinterpret_cast<const float4*>(wn + (n0 - group * p.norm_width));
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 w4 = __ldg(wp + q);
-              const float2 a = unpack_bf16x2(pk[c][2 * q]);
-              const float2 b = unpack_bf16x2(pk[c][2 * q + 1]);
-              v[4 * q] = bf16_round(bf16_round(a.x * rms) * w4.x);
-              v[4 * q + 1] = bf16_round(bf16_round(a.y * rms) * w4.y);
-              v[4 * q + 2] = bf16_round(bf16_round(b.x * rms) * w4.z);
-              v[4 * q + 3] = bf16_round(bf16_round(b.y * rms) * w4.w);
-            }
-            if (do_rope) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const float e = v[2 * i], o = v[2 * i + 1];
-                v[2 * i] = e * cs_cur[i] - o * sn_cur[i];
-                v[2 * i + 1] = e * sn_cur[i] + o * cs_cur[i];
-              }
-            }
-            uint32_t w[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-            if (row_ok) {
-              uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) + (static_cast<size_t>(row) * p.ldo + n0) * 2;
-#pragma unroll
-              for (int q = 0; q < 4; ++q) st_global_v4(dst + 16 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-            }
-          }
-          continue;
-        }
-
-        // Plain tiles (all of gemm_act, the unnormalized column groups of the norm GEMM).
-#pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
-          const int n0 = n_blk * BN + col_base + c * 32;
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
-          if (c == kChunks - 1) {
-            release_acc(buf);
-          }
-          if (n0 >= s.N) continue;  // uniform inside the half
-          finish_linear(v, n0);
-          if (KIND == kEpiAct && p.act == 1) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+            for (int j = 0; j < 16; ++j) gelu_tanh2(v[2 * j], v[2 * j + 1]);
           }
           uint32_t w[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-          // Stage 128 rows x 32 bf16 (64-byte swizzle) and store with TMA.
-          if (ht == 0) bulk_wait_read<1>();
-          named_bar_sync(bar_half, kEpiThreads);
-          const uint32_t rowa = stg_half + sbuf * kStgBytes + r * 64;
+          if (ss_on) {
+            // WanRMSNorm normalizes the bf16 Linear output: square the rounded values.
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float2 f = unpack_bf16x2(w[j]);
+              const uint64_t f2 = f2_pack(f.x, f.y);
+              ss2 = ffma2(f2, f2, ss2);
+            }
+          }
+          // Stage the warp's 32 rows x 32 bf16 (64-byte swizzle) and store them with TMA.
+          if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+          __syncwarp();
+          const uint32_t rowa = stg_warp + sbuf * kWarpStgBytes + lane * 64;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            st_shared_v4(rowa + ((q ^ ((r >> 1) & 3)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+            st_shared_v4(rowa + ((q ^ ((lane >> 1) & 3)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
           }
           fence_proxy_async_smem();
-          named_bar_sync(bar_half, kEpiThreads);
-          if (ht == 0) {
-            if (rows_any) tma_store_2d(&tmOut, stg_half_ptr + sbuf * kStgBytes, n0, m_blk * BM);
+          __syncwarp();
+          if (lane == 0) {
+            if (rows_any) tma_store_2d(&tmOut, stg_warp_ptr + sbuf * kWarpStgBytes, n0, warp_row0);
             bulk_commit();
           }
           sbuf ^= 1;
         }
+        if (ss_on && row_ok) {
+          float s0, s1;
+          f2_unpack(ss2, s0, s1);
+          p.ss_part[static_cast<size_t>(row) * p.ss_ld + (nh >> 7)] = (s0 + s1) * (1.f / 128.f);
+        }
       }
-      if (KIND == kEpiNorm && !failed) {
-        named_bar_sync(3, 2 * kEpiThreads);
-        release_pending();
-      }
-      if (ht == 0) bulk_wait_all<0>();
+      if (lane == 0) bulk_wait_all<0>();
     } else if (half == 0) {
       // ----------------------------- residual -----------------------------
       const int et = ht;
@@ -850,8 +711,7 @@ int g_cta_pair = 1;
 
 template <int KIND, bool PAIR>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const CUtensorMap& c,
-           const CUtensorMap& x, const GemmShape& shape, const EpiParams& p, cudaStream_t stream, bool cooperative,
-           int max_ctas, int min_grid = 1) {
+           const CUtensorMap& x, const GemmShape& shape, const EpiParams& p, cudaStream_t stream, int max_ctas) {
   static bool attr_set[64] = {};
   static int pair_slots[64] = {};  // co-resident CTA pairs per device
   int dev = 0;
@@ -861,15 +721,13 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, con
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = cooperative ? 1 : 0;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = PAIR ? 2 : 1;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = PAIR ? 2 : 1;
+  cfg.numAttrs = PAIR ? 1 : 0;
   if (!attr_set[dev & 63]) {
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
@@ -892,20 +750,9 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, con
     if (2 * s.tiles < grid) grid = 2 * s.tiles;
   } else {
     if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
-    if (max_ctas <= 0 && min_grid > 1 && s.tiles > grid) {
-      // Norm epilogue: a multiple of the group size keeps a group's tiles in one wave (no
-      // waiting on the next wave), and a grid that is not a multiple of the column-tile count
-      // rotates every CTA through normalized and plain tiles (their epilogue costs differ).
-      int g = grid - grid % min_grid;
-      while (g > min_grid && p.norm_groups * min_grid < s.n_blocks && g % s.n_blocks == 0) g -= min_grid;
-      if (g >= min_grid) grid = g;
-    }
     if (s.tiles < grid) grid = s.tiles;
   }
   if (grid <= 0) return WDIT_OK;
-  // The cross-tile exchange of the norm epilogue needs the tiles of one group on distinct,
-  // co-resident CTAs: a grid smaller than the group would wait on its own later tile.
-  if (grid < min_grid) return WDIT_ERR_ARG;
   cfg.gridDim = dim3(grid);
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, PAIR>, a, b, o, c, x, s, p);
   return e == cudaSuccess ? WDIT_OK : WDIT_ERR_CUDA_BASE + static_cast<int>(e);
@@ -960,6 +807,70 @@ int ln_fill(LnFold* ln, const float* csum, const float* stats, int stats_tiles, 
   return WDIT_OK;
 }
 
+// RMSNorm partials: one fp32 mean square per row and 128-column block of the normalized
+// groups, rows of norm_groups * norm_width / 128 entries (256-byte rounded).
+long long norm_partials_bytes(int M, int norm_groups, int norm_width) {
+  const long long cols = static_cast<long long>(norm_groups) * (norm_width / 128);
+  return ((static_cast<long long>(M) * cols * 4 + 255) / 256) * 256;
+}
+
+int check_norm(const void* A, int lda, const void* B, int ldb, const void* out, int ldo, int M, int N, int K,
+               const float* vec, int norm_groups, int norm_width, const float* norm_w0, const float* norm_w1,
+               int rope_groups, const float* rope_cos, const float* rope_sin, int rope_ld, int rows_per_batch,
+               int token_offset) {
+  int rc = check_common(A, lda, B, ldb, M, N, K);
+  if (rc) return rc;
+  if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
+  if (!aligned16(out) || ldo % 8 != 0) return WDIT_ERR_ALIGN;
+  if (norm_groups < 0 || norm_groups > 2 || rope_groups < 0 || rope_groups > norm_groups) return WDIT_ERR_ARG;
+  if (norm_groups > 0) {
+    if (norm_width <= 0 || norm_width % 128 != 0 || norm_groups * norm_width > N) return WDIT_ERR_SHAPE;
+    if (norm_w0 == nullptr || (norm_groups > 1 && norm_w1 == nullptr)) return WDIT_ERR_ARG;
+    if (!aligned16(norm_w0) || (norm_w1 && !aligned16(norm_w1))) return WDIT_ERR_ALIGN;
+  }
+  if (rope_groups > 0) {
+    // token-major tables: entry (token, pair) at token * rope_ld + pair, 64 pairs per head
+    if (rope_cos == nullptr || rope_sin == nullptr || rows_per_batch <= 0 || token_offset < 0) return WDIT_ERR_ARG;
+    if (rope_ld < 64) return WDIT_ERR_SHAPE;
+    if (!aligned16(rope_cos) || !aligned16(rope_sin) || rope_ld % 4 != 0) return WDIT_ERR_ALIGN;
+  }
+  if (vec != nullptr && !aligned16(vec)) return WDIT_ERR_ALIGN;
+  return WDIT_OK;
+}
+
+// GEMM (bias / absorbed LayerNorm, bf16 out, RMSNorm partials) followed by the in-place
+// RMSNorm / RoPE pass over the normalized column groups.
+int run_norm(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+             const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles, int ln_stats_width,
+             float ln_eps, int norm_groups, int norm_width, const float* norm_w0, const float* norm_w1,
+             float norm_eps, int rope_groups, const float* rope_cos, const float* rope_sin, int rope_ld,
+             int rows_per_batch, int token_offset, float* part, cudaStream_t stream, int max_ctas) {
+  EpiParams p = {};
+  int rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
+  if (rc) return rc;
+  p.vec = vec;
+  p.rows_per_batch = M;
+  p.has_out_map = 1;
+  if (norm_groups > 0) {
+    p.ss_part = part;
+    p.ss_ld = norm_groups * (norm_width / 128);
+    p.ss_cols = norm_groups * norm_width;
+  }
+  const bool pair = use_pair(M);
+  CUtensorMap ma, mb, mo, none;
+  memset(&none, 0, sizeof(none));
+  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K, pair))) return rc;
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
+    return rc;
+  const GemmShape shape = make_shape(M, N, K);
+  rc = pair ? launch<kEpiAct, true>(ma, mb, mo, none, none, shape, p, stream, max_ctas)
+            : launch<kEpiAct, false>(ma, mb, mo, none, none, shape, p, stream, max_ctas);
+  if (rc || norm_groups == 0) return rc;
+  return launch_rms_rope_apply(out, ldo, M, part, p.ss_ld, norm_groups, norm_width, norm_w0, norm_w1, norm_eps,
+                               rope_groups, rope_cos, rope_sin, rope_ld, rows_per_batch > 0 ? rows_per_batch : M,
+                               token_offset, stream);
+}
+
 }  // namespace
 }  // namespace wdit
 
@@ -1004,12 +915,15 @@ int wdit_read_error(unsigned int* out4, int clear) {
 
 int wdit_gemm_act(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
                   const float* vec, int act, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
-                  int ln_stats_width, float ln_eps, void* stream, int max_ctas) {
+                  int ln_stats_width, float ln_eps, float* ms_out, int ms_ld, int ms_cols, void* stream,
+                  int max_ctas) {
   int rc = check_common(A, lda, B, ldb, M, N, K);
   if (rc) return rc;
   if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
   if (act != 0 && act != 1) return WDIT_ERR_ARG;
   if (vec != nullptr && !aligned16(vec)) return WDIT_ERR_ALIGN;
+  if (ms_out != nullptr && (ms_cols <= 0 || ms_cols % 128 != 0 || ms_cols > N || ms_ld < ms_cols / 128))
+    return WDIT_ERR_SHAPE;
   EpiParams p = {};
   rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
   if (rc) return rc;
@@ -1017,17 +931,20 @@ int wdit_gemm_act(const void* A, int lda, const void* B, int ldb, void* out, int
   p.act = act;
   p.rows_per_batch = M;
   p.has_out_map = 1;
+  p.ss_part = ms_out;
+  p.ss_ld = ms_ld;
+  p.ss_cols = ms_out != nullptr ? ms_cols : 0;
   CUtensorMap ma, mb, mo, none;
   memset(&none, 0, sizeof(none));
   const bool pair = use_pair(M);
   if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K, pair))) return rc;
-  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
   if (pair)
     return launch<kEpiAct, true>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
-                                 false, max_ctas);
+                                 max_ctas);
   return launch<kEpiAct, false>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
-                                false, max_ctas);
+                                max_ctas);
 }
 
 int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const float* C, int ldc, float* out, int ldo,
@@ -1082,74 +999,35 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
     return rc;
   const GemmShape shape = make_shape(M, N, K);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (pair) return launch<kEpiResidualLongK, true>(ma, mb, mo, mc, mx, shape, p, st, false, max_ctas);
-  if (long_k) return launch<kEpiResidualLongK, false>(ma, mb, mo, mc, mx, shape, p, st, false, max_ctas);
-  return launch<kEpiResidual, false>(ma, mb, mo, mc, mx, shape, p, st, false, max_ctas);
+  if (pair) return launch<kEpiResidualLongK, true>(ma, mb, mo, mc, mx, shape, p, st, max_ctas);
+  if (long_k) return launch<kEpiResidualLongK, false>(ma, mb, mo, mc, mx, shape, p, st, max_ctas);
+  return launch<kEpiResidual, false>(ma, mb, mo, mc, mx, shape, p, st, max_ctas);
 }
 
 long long wdit_gemm_norm_workspace_bytes(int M, int N, int norm_groups, int norm_width) {
   if (M <= 0 || norm_groups <= 0 || norm_width <= 0) return 0;
-  const long long part_cols = static_cast<long long>(norm_groups) * (norm_width / BN);
-  const long long part = ((static_cast<long long>(M) * part_cols * 4 + 255) / 256) * 256;
   (void)N;
-  return kCounterRegionBytes + part;
+  return norm_partials_bytes(M, norm_groups, norm_width);
 }
 
 int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
                    const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
                    int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
                    const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos, const float* rope_sin,
-                   int rope_ld, int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes, void* stream,
-                   int max_ctas) {
-  int rc = check_common(A, lda, B, ldb, M, N, K);
+                   int rope_ld, int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes,
+                   void* stream, int max_ctas) {
+  int rc = check_norm(A, lda, B, ldb, out, ldo, M, N, K, vec, norm_groups, norm_width, norm_w0, norm_w1, rope_groups,
+                      rope_cos, rope_sin, rope_ld, rows_per_batch, token_offset);
   if (rc) return rc;
-  if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
-  if (norm_groups < 0 || norm_groups > 2 || rope_groups < 0 || rope_groups > norm_groups) return WDIT_ERR_ARG;
   if (norm_groups > 0) {
-    if (norm_width <= 0 || norm_width % BN != 0 || norm_groups * norm_width > N) return WDIT_ERR_SHAPE;
-    if (norm_w0 == nullptr || (norm_groups > 1 && norm_w1 == nullptr)) return WDIT_ERR_ARG;
-    if (!aligned16(norm_w0) || (norm_w1 && !aligned16(norm_w1))) return WDIT_ERR_ALIGN;
-    if (workspace == nullptr || workspace_bytes < wdit_gemm_norm_workspace_bytes(M, N, norm_groups, norm_width))
+    if (workspace == nullptr || workspace_bytes < norm_partials_bytes(M, norm_groups, norm_width))
       return WDIT_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return WDIT_ERR_ALIGN;
   }
-  if (rope_groups > 0) {
-    if (rope_cos == nullptr || rope_sin == nullptr || rows_per_batch <= 0 || token_offset < 0) return WDIT_ERR_ARG;
-    if (rope_ld < rows_per_batch + token_offset) return WDIT_ERR_SHAPE;
-    if (!aligned16(rope_cos) || !aligned16(rope_sin)) return WDIT_ERR_ALIGN;
-    if (norm_width % 128 != 0) return WDIT_ERR_SHAPE;
-  }
-  if (vec != nullptr && !aligned16(vec)) return WDIT_ERR_ALIGN;
-  EpiParams p = {};
-  rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
-  if (rc) return rc;
-  p.vec = vec;
-  p.norm_groups = norm_groups;
-  p.norm_width = norm_groups > 0 ? norm_width : BN;
-  p.norm_w[0] = norm_w0;
-  p.norm_w[1] = norm_w1;
-  p.norm_eps = norm_eps;
-  p.rope_groups = rope_groups;
-  p.rope_cos = rope_cos;
-  p.rope_sin = rope_sin;
-  p.rope_ld = rope_ld;
-  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
-  p.token_offset = token_offset;
-  p.has_out_map = 1;
-  p.out = out;
-  p.ldo = ldo;
-  if (norm_groups > 0) {
-    if (static_cast<long long>((M + BM - 1) / BM) * norm_groups * 4 > kCounterRegionBytes) return WDIT_ERR_SHAPE;
-    p.counters = reinterpret_cast<unsigned int*>(workspace);
-    p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kCounterRegionBytes);
-  }
-  CUtensorMap ma, mb, mo, none;
-  memset(&none, 0, sizeof(none));
-  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
-  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
-    return rc;
-  return launch<kEpiNorm, false>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream),
-                          norm_groups > 0, max_ctas, norm_groups > 0 ? norm_width / BN : 1);
+  return run_norm(A, lda, B, ldb, out, ldo, M, N, K, vec, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, ln_eps,
+                  norm_groups, norm_width, norm_w0, norm_w1, norm_eps, rope_groups, rope_cos, rope_sin, rope_ld,
+                  rows_per_batch, token_offset, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream),
+                  max_ctas);
 }
 
 }  // extern "C"
@@ -1161,18 +1039,16 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
 // that executes inside a region where allocation is not permitted (for example while
 // another component is recording work for replay, or inside a fixed memory budget that
 // was reserved up front), and hosts whose allocator is owned by a different runtime and
-// is not reachable from the call site. For them the row-statistics scratch lives in a
-// fixed, file-scope device array instead of a caller-supplied workspace.
+// is not reachable from the call site. For them the RMSNorm partials live in a fixed,
+// file-scope device array instead of a caller-supplied workspace.
 //
 // Limits and sharing rules:
 //   * The array holds WDIT_STATIC_SCRATCH_BYTES (4 MiB) on every GPU that loads this
 //     library, for the lifetime of the process.
 //   * A call needs wdit_gemm_norm_workspace_bytes(M, N, norm_groups, norm_width) bytes of
 //     it; larger problems are rejected with WDIT_ERR_SCRATCH_LIMIT before any launch.
-//   * All calls on a device share the one array and it keeps the last call's contents.
-//     The arrival counters must start at zero, so each call clears them (cudaMemsetAsync
-//     on the caller's stream) before its launch; calls that overlap on the GPU (different
-//     streams with no ordering between them) race on the array.
+//   * All calls on a device share the one array; calls that overlap on the GPU (different
+//     streams with no ordering between them) race on it.
 //   * The first call on a device looks the array's device address up once
 //     (cudaGetSymbolAddress, with that device current); make that first call before any
 //     stream capture begins.
@@ -1215,58 +1091,18 @@ int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* 
                           const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
                           const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream,
                           int max_ctas) {
-  int rc = check_common(A, lda, B, ldb, M, N, K);
+  if (norm_groups < 1) return WDIT_ERR_ARG;
+  int rc = check_norm(A, lda, B, ldb, out, ldo, M, N, K, vec, norm_groups, norm_width, norm_w0, norm_w1, rope_groups,
+                      rope_cos, rope_sin, rope_ld, rows_per_batch, token_offset);
   if (rc) return rc;
-  if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
-  if (norm_groups < 1 || norm_groups > 2 || rope_groups < 0 || rope_groups > norm_groups) return WDIT_ERR_ARG;
-  if (norm_width <= 0 || norm_width % BN != 0 || norm_groups * norm_width > N) return WDIT_ERR_SHAPE;
-  if (norm_w0 == nullptr || (norm_groups > 1 && norm_w1 == nullptr)) return WDIT_ERR_ARG;
-  if (!aligned16(norm_w0) || (norm_w1 && !aligned16(norm_w1))) return WDIT_ERR_ALIGN;
-  if (rope_groups > 0) {
-    if (rope_cos == nullptr || rope_sin == nullptr || rows_per_batch <= 0 || token_offset < 0) return WDIT_ERR_ARG;
-    if (rope_ld < rows_per_batch + token_offset) return WDIT_ERR_SHAPE;
-    if (!aligned16(rope_cos) || !aligned16(rope_sin)) return WDIT_ERR_ALIGN;
-    if (norm_width % 128 != 0) return WDIT_ERR_SHAPE;
-  }
-  if (vec != nullptr && !aligned16(vec)) return WDIT_ERR_ALIGN;
-  const long long need = wdit_gemm_norm_workspace_bytes(M, N, norm_groups, norm_width);
-  if (need > static_cast<long long>(WDIT_STATIC_SCRATCH_BYTES)) return WDIT_ERR_SCRATCH_LIMIT;
+  if (norm_partials_bytes(M, norm_groups, norm_width) > static_cast<long long>(WDIT_STATIC_SCRATCH_BYTES))
+    return WDIT_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   if ((rc = static_scratch_address(&scratch))) return rc;
-
-  EpiParams p = {};
-  rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
-  if (rc) return rc;
-  p.vec = vec;
-  p.norm_groups = norm_groups;
-  p.norm_width = norm_width;
-  p.norm_w[0] = norm_w0;
-  p.norm_w[1] = norm_w1;
-  p.norm_eps = norm_eps;
-  p.rope_groups = rope_groups;
-  p.rope_cos = rope_cos;
-  p.rope_sin = rope_sin;
-  p.rope_ld = rope_ld;
-  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
-  p.token_offset = token_offset;
-  p.has_out_map = 1;
-  p.out = out;
-  p.ldo = ldo;
-  const long long ctr_bytes = static_cast<long long>((M + BM - 1) / BM) * norm_groups * 4;
-  if (ctr_bytes > kCounterRegionBytes) return WDIT_ERR_SHAPE;
-  p.counters = reinterpret_cast<unsigned int*>(scratch);
-  p.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCounterRegionBytes);
-  // The counters start every launch at zero (the array keeps whatever the last call left).
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, static_cast<size_t>(ctr_bytes), static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
-
-  CUtensorMap ma, mb, mo, none;
-  memset(&none, 0, sizeof(none));
-  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K))) return rc;
-  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, BM, CU_TENSOR_MAP_SWIZZLE_64B)))
-    return rc;
-  return launch<kEpiNorm, false>(ma, mb, mo, none, none, make_shape(M, N, K), p, static_cast<cudaStream_t>(stream), true,
-                          max_ctas, norm_width / BN);
+  return run_norm(A, lda, B, ldb, out, ldo, M, N, K, vec, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, ln_eps,
+                  norm_groups, norm_width, norm_w0, norm_w1, norm_eps, rope_groups, rope_cos, rope_sin, rope_ld,
+                  rows_per_batch, token_offset, static_cast<float*>(scratch), static_cast<cudaStream_t>(stream),
+                  max_ctas);
 }
 
 }  // extern "C"

@@ -23,30 +23,28 @@ struct EpiParams {
   const float* vec;  // per-column bias / shift term [N], nullable
   LnFold ln;
   int act;  // kEpiAct: 0 = identity, 1 = tanh-GELU
-  // residual epilogue
+  // kEpiAct: per-row mean of squares of the bf16 output over each 128-column block of the
+  // leading ss_cols columns -> ss_part[row * ss_ld + block] (the RMSNorm partials), nullable
+  float* ss_part;
+  int ss_ld;
+  int ss_cols;
+  // residual epilogues
   const float* gate_a;  // [N], nullable (no gate)
   const float* gate_b;  // [batches, gate_b_stride], nullable; gate = gate_a + gate_b[batch]
   int gate_b_stride;
-  int rows_per_batch;  // rows of one batch entry along M (per-batch vectors, RoPE token index)
+  int rows_per_batch;  // rows of one batch entry along M (per-batch gate rows)
   float* stats_out;    // [M, ceil(N/256), 2], nullable
-  // norm epilogue
-  int norm_groups;  // leading column groups of width norm_width that get the full-width RMSNorm
-  int norm_width;
-  const float* norm_w[2];
-  float norm_eps;
-  int rope_groups;  // leading groups that also get 3D RoPE
-  const float* rope_cos;
-  const float* rope_sin;
-  int rope_ld;  // pair-major tables: entry (pair, token) at pair * rope_ld + token
-  int token_offset;
-  float* part;             // scratch [M, norm_groups * norm_width/256]
-  unsigned int* counters;  // scratch [m_blocks * norm_groups], zero between launches
-  void* out;  // norm epilogue: direct bf16 stores
-  int ldo;
-  void* x_out;  // residual epilogue: bf16 copy of the result (direct stores)
+  void* x_out;         // bf16 copy of the result (long-K variant: direct stores)
   int ldx;
   int has_out_map;
   int has_x_map;
 };
+
+// In-place full-width RMSNorm (+ RoPE) of the leading column groups of a bf16 matrix from
+// per-128-column mean-square partials (aux.cu). RoPE tables are token-major: entry
+// (token, pair) at token * rope_ld + pair; row r is token r % rows_per_batch + token_offset.
+int launch_rms_rope_apply(void* x, int ldx, int M, const float* part, int part_ld, int groups, int width,
+                          const float* w0, const float* w1, float eps, int rope_groups, const float* rope_cos,
+                          const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream);
 
 }  // namespace wdit

@@ -137,7 +137,7 @@ def run(M: int = 32760, only: set[str] | None = None, iters: int = 20, cublas: b
         s = rnd((D,), 0.1, torch.float32)
         wf, cs, vec = ops.fold_weight(w, mult_c=1.0, mult_a=s, shift_a=s)
         ang = rnd((M, 64), 3.0, torch.float32)
-        cos, sin = torch.cos(ang).t().contiguous(), torch.sin(ang).t().contiguous()  # pair-major
+        cos, sin = torch.cos(ang), torch.sin(ang)  # token-major [M, 64]
         nw = 1.0 + rnd((D,), 0.1, torch.float32)
         out = torch.empty((M, 3 * D), dtype=torch.bfloat16, device=dev)
         ln = ops.LnFold(cs, stats, 1e-6)

@@ -106,8 +106,13 @@ def _ln_args(ln: LnFold | None, K: int):
     return (ptr(ln.csum), ptr(ln.stats), stats_tiles(K), STATS_WIDTH, ln.eps)
 
 
-def gemm_act(a, w, *, vec=None, act="none", ln: LnFold | None = None, out=None, max_ctas=0):
-    """out[M,N] bf16 = act(LN(a @ w.T) + vec). a bf16 [M,K]; w bf16 [N,K]."""
+def gemm_act(a, w, *, vec=None, act="none", ln: LnFold | None = None, out=None, ms_out=None, ms_cols=0,
+             max_ctas=0):
+    """out[M,N] bf16 = act(LN(a @ w.T) + vec). a bf16 [M,K]; w bf16 [N,K].
+
+    ms_out [M, >= ms_cols/128] fp32 (optional): mean of bf16(out)^2 over each 128-column block of
+    the leading ms_cols columns (RMSNorm partials).
+    """
     _require_cuda(a, w)
     a = _rowmajor(a)
     M, K = a.shape
@@ -117,10 +122,15 @@ def gemm_act(a, w, *, vec=None, act="none", ln: LnFold | None = None, out=None, 
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     vec = _f32vec(vec)
+    ms_ld = 0
+    if ms_out is not None:
+        assert ms_out.dtype == torch.float32 and ms_out.stride(1) == 1 and ms_out.shape[0] == M
+        ms_ld = ms_out.stride(0)
     call(
         "wdit_gemm_act",
         ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(out), out.stride(0), M, N, K,
-        ptr(vec), _ACT[act], *_ln_args(ln, K), stream_ptr(), max_ctas,
+        ptr(vec), _ACT[act], *_ln_args(ln, K), ptr(ms_out), ms_ld, ms_cols if ms_out is not None else 0,
+        stream_ptr(), max_ctas,
     )
     return out
 
@@ -153,12 +163,12 @@ def gemm_residual(a, w, c, *, out=None, bias=None, gate_a=None, gate_b=None, gat
 
 def norm_workspace(M: int, N: int, norm_groups: int, norm_width: int, device) -> torch.Tensor:
     nbytes = int(_lib.load().wdit_gemm_norm_workspace_bytes(M, N, norm_groups, norm_width))
-    return torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+    return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
 
 
 class Workspace:
-    """Grow-only scratch for gemm_norm (the arrival counters must start at zero; the kernel
-    leaves them at zero after every successful launch)."""
+    """Grow-only scratch for gemm_norm's RMSNorm partials (no initialization needed; launches
+    on one stream may share it)."""
 
     def __init__(self):
         self.buf: torch.Tensor | None = None
@@ -166,12 +176,8 @@ class Workspace:
     def get(self, M, N, groups, width, device) -> torch.Tensor:
         need = int(_lib.load().wdit_gemm_norm_workspace_bytes(M, N, groups, width))
         if self.buf is None or self.buf.numel() < need or self.buf.device != torch.device(device):
-            self.buf = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
+            self.buf = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
         return self.buf
-
-    def reset(self) -> None:
-        if self.buf is not None:
-            self.buf.zero_()
 
 
 _default_ws: dict[int, Workspace] = {}
@@ -189,7 +195,8 @@ def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_w
               out=None, workspace: Workspace | None = None, max_ctas=0):
     """out[M,N] bf16 = RoPE(RMSNorm_fullwidth(bf16(LN(a @ w.T) + vec))) per column group.
 
-    rope_cos / rope_sin are pair-major [64, T] fp32 tables (row = rotary pair, column = token).
+    rope_cos / rope_sin are token-major [T, 64] fp32 tables (row = token, column = rotary pair;
+    any row stride that is a multiple of 4), as build_wan_rope_table returns them.
     """
     _require_cuda(a, w)
     a = _rowmajor(a)
@@ -208,15 +215,17 @@ def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_w
     vec = _f32vec(vec)
     rope_ld = 0
     if rope_groups > 0:
-        assert rope_cos.shape == rope_sin.shape and rope_cos.shape[0] == HEAD_DIM // 2
-        assert rope_cos.is_contiguous() and rope_sin.is_contiguous() and rope_cos.dtype == torch.float32
-        rope_ld = rope_cos.shape[1]
+        assert rope_cos.shape == rope_sin.shape and rope_cos.shape[1] == HEAD_DIM // 2
+        assert rope_cos.dtype == torch.float32 and rope_sin.dtype == torch.float32
+        assert rope_cos.stride(1) == 1 and rope_sin.stride() == rope_cos.stride()
+        assert rope_cos.shape[0] >= (rows_per_batch or M) + token_offset, "RoPE tables shorter than the tokens"
+        rope_ld = rope_cos.stride(0)
     call(
         "wdit_gemm_norm",
         ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(out), out.stride(0), M, N, K,
         ptr(vec), *_ln_args(ln, K), norm_groups, norm_width, ptr(w0), ptr(w1), float(norm_eps),
         rope_groups, ptr(rope_cos), ptr(rope_sin), rope_ld, rows_per_batch, token_offset, ptr(ws), nbytes,
-        stream_ptr(), max_ctas,
+        stream_ptr(), max_ctas, kernels=2 if norm_groups > 0 else 1,
     )
     return out
 
@@ -293,9 +302,9 @@ def qk_linear_bias_partial_rms(a, qk_weight_kn, qk_bias, block_size: int = RMS_B
     assert qk_weight_kn.shape == (k, 2 * DIM)
     assert qk_bias.shape == (2 * DIM,)
     assert (2 * DIM) % block_size == 0
-    qk = gemm_act(a, _weight_nk(qk_weight_kn), vec=qk_bias, act="none")
+    assert block_size == RMS_BLOCK, "partials are per 128-column block"
     partial = torch.empty((m, 2 * DIM // block_size), dtype=torch.float32, device=a.device)
-    call("wdit_block_mean_sq", ptr(qk), qk.stride(0), m, 2 * DIM, block_size, ptr(partial), stream_ptr())
+    qk = gemm_act(a, _weight_nk(qk_weight_kn), vec=qk_bias, act="none", ms_out=partial, ms_cols=2 * DIM)
     return qk, partial
 
 
@@ -330,7 +339,7 @@ def qk_coda_rms_rope(a, qk_weight_kn, qk_bias, q_weight, k_weight, cos, sin, eps
     assert cos.shape == sin.shape == (m, HEAD_DIM // 2)
     qk = gemm_norm(
         a, _weight_nk(qk_weight_kn), vec=qk_bias, norm_groups=2, norm_width=DIM, norm_w=(q_weight, k_weight),
-        norm_eps=eps, rope_groups=2, rope_cos=cos.float().t().contiguous(), rope_sin=sin.float().t().contiguous(),
+        norm_eps=eps, rope_groups=2, rope_cos=cos.float().contiguous(), rope_sin=sin.float().contiguous(),
         rows_per_batch=m, token_offset=0,
     )
     return qk[:, :DIM], qk[:, DIM:]
@@ -366,12 +375,6 @@ def _rope_table(grid_fhw, freqs: torch.Tensor, pair_major: bool):
 def build_wan_rope_table(grid_fhw, freqs: torch.Tensor):
     """Shared per-token cos/sin [f*h*w, 64] fp32 tables.  wan_coda_kernels.py:414-430."""
     return _rope_table(grid_fhw, freqs, pair_major=False)
-
-
-def build_rope_table_pair_major(grid_fhw, freqs: torch.Tensor):
-    """The same tables transposed to [64, f*h*w] (what the fused QKV epilogue reads: a warp's
-    consecutive tokens load one contiguous line per rotary pair)."""
-    return _rope_table(grid_fhw, freqs, pair_major=True)
 
 
 def replace_parameter_with_view(module: nn.Module, name: str, view: torch.Tensor) -> None:

@@ -75,12 +75,16 @@ int wdit_read_error(unsigned int* out4, int clear);
  * LN is the absorbed adaLN LayerNorm: rstd_m * (acc - mu_m * ln_csum[n]) where (mu, rstd) of
  * row m are merged from ln_stats[m, 0..ln_stats_tiles-1] = (mean, M2) over ln_stats_width
  * columns each (as written by wdit_gemm_residual / wdit_ln_stats); ln_csum = NULL disables it.
+ * ms_out (nullable): ms_out[m * ms_ld + j] = mean over the 128 columns [128j, 128j+128) of
+ * bf16(out)^2 for the leading ms_cols columns (ms_cols % 128 == 0), the RMSNorm partials.
  * Replaces: coda_wan/wan_coda_kernels.py:120-152 linear_bias_gelu_fixed (EVTGELUBias :84-105)
- * together with the LN+modulate kernel it consumes (:35-81, removed by the fold).
+ * together with the LN+modulate kernel it consumes (:35-81, removed by the fold); with ms_out,
+ * :192-230 qk_linear_bias_partial_rms (EVTColBlockReductionStore with the mean-square op).
  */
 int wdit_gemm_act(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
                   const float* vec, int act, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
-                  int ln_stats_width, float ln_eps, void* stream, int max_ctas);
+                  int ln_stats_width, float ln_eps, float* ms_out, int ms_ld, int ms_cols, void* stream,
+                  int max_ctas);
 
 /*
  * out[M,N] (fp32) = C + (A . B^T + bias) * gate,  gate[m, n] = gate_a[n] + gate_b[batch(m), n]
@@ -95,18 +99,20 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
                        int gate_b_stride, int rows_per_batch, void* x_bf16_out, int ldx, float* stats_out,
                        void* stream, int max_ctas);
 
-/* Workspace bytes wdit_gemm_norm needs: a fixed 64 KiB region of arrival counters at offset 0
- * (zero before the first launch; every successful launch leaves it zero, so one workspace can
- * serve launches of any shape) followed by the per-row partials. */
+/* Workspace bytes wdit_gemm_norm needs: the RMSNorm partials, M x norm_groups * norm_width / 128
+ * fp32 (rounded up to 256 bytes). Contents need no initialization. */
 long long wdit_gemm_norm_workspace_bytes(int M, int N, int norm_groups, int norm_width);
 
 /*
  * out[M,N] (bf16): y = LN(A . B^T) + vec, rounded to bf16; columns [g*W, (g+1)*W) for
- * g < norm_groups get the full-width WanRMSNorm bf16(bf16(y * rsqrt(mean_W(y^2) + eps)) * w_g),
- * and for g < rope_groups the interleaved-pair 3D RoPE with the pair-major tables
- * rope_cos/sin[pair * rope_ld + token] (pair < 64, token = m % rows_per_batch + token_offset,
- * rope_ld >= rows_per_batch + token_offset). Remaining columns are stored as bf16(y).
+ * g < norm_groups (W % 128 == 0) get the full-width WanRMSNorm
+ * bf16(bf16(y * rsqrt(mean_W(y^2) + eps)) * w_g), and for g < rope_groups the interleaved-pair
+ * 3D RoPE of 128-column heads with the token-major tables rope_cos/sin[token * rope_ld + pair]
+ * (pair < 64, rope_ld >= 64, token = m % rows_per_batch + token_offset; the tables must hold
+ * rows_per_batch + token_offset tokens). Remaining columns are stored as bf16(y).
  * QKV: norm_groups 2, rope_groups 2; cross-Q: 1, 0; cross-KV: 1, 0.
+ * Two launches on `stream`: the GEMM (bf16 y plus the mean-square partials, in the workspace)
+ * and an in-place RMSNorm / RoPE pass over the normalized groups.
  * Replaces: coda_wan/wan_coda_kernels.py:355-368 qk_coda_rms_rope (= :192-230
  * qk_linear_bias_partial_rms + :313-352 qk_rms_rope_from_partials), the V projection at
  * coda_wan/run_wan_coda.py:158, and :371-411 rmsnorm_fused applied to cross-attention q / k.
@@ -123,13 +129,12 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
  * the caller. No counterpart in the reference (which always allocates through PyTorch); it is
  * for callers that cannot allocate device memory where they issue this GEMM, e.g. code running
  * where allocation is not allowed or with an allocator owned by another runtime.
- * Same arguments and result as wdit_gemm_norm (norm_groups >= 1). The row-statistics scratch
- * is a fixed array of WDIT_STATIC_SCRATCH_BYTES (4 MiB) per GPU, held for the life of the
+ * Same arguments and result as wdit_gemm_norm (norm_groups >= 1). The RMSNorm partials live
+ * in a fixed array of WDIT_STATIC_SCRATCH_BYTES (4 MiB) per GPU, held for the life of the
  * process; problems needing more (wdit_gemm_norm_workspace_bytes > 4 MiB, e.g. QKV beyond
- * ~86k rows) return WDIT_ERR_SCRATCH_LIMIT. Every call on a device shares that array: calls
- * that overlap on the GPU race. Each call zeroes the array's counters on `stream` first. The
- * first call on a device looks the array's address up (with this library's current device,
- * see wdit_set_device); make it before any stream capture.
+ * ~43k rows) return WDIT_ERR_SCRATCH_LIMIT. Every call on a device shares that array: calls
+ * that overlap on the GPU race. The first call on a device looks the array's address up (with
+ * this library's current device, see wdit_set_device); make it before any stream capture.
  */
 int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
                           const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
@@ -199,13 +204,6 @@ int wdit_qk_rms_rope_from_partials(void* qk, int ldqk, const float* partial, int
  */
 int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, int pair_major, float* cos_out,
                     float* sin_out, void* stream);
-
-/*
- * Mean of squares of x[M,N] (bf16) over consecutive column blocks: out[M, N/block] (fp32).
- * Replaces: the partial output of coda_wan/wan_coda_kernels.py:192-230
- * qk_linear_bias_partial_rms (EVTColBlockReductionStore with the mean-square op).
- */
-int wdit_block_mean_sq(const void* x, int ldx, int M, int N, int block, float* out, void* stream);
 
 /* ---- sequence-parallel (Ulysses) regrouping; no reference counterpart (the reference is
  * single-GPU), these serve the token-sharded multi-GPU forward ----

@@ -43,12 +43,15 @@ def test_library_is_built_for_sm100a():
 def test_argument_validation_without_device(lib):
     null = ctypes.c_void_p(None)
     # NULL operands -> WDIT_ERR_ARG; bad shapes -> WDIT_ERR_SHAPE; no CUDA call is reached.
-    assert lib.wdit_gemm_act(null, 64, null, 64, null, 64, 128, 256, 64, null, 0, null, null, 0, 0, 0.0, null, 0) == 1
+    assert lib.wdit_gemm_act(null, 64, null, 64, null, 64, 128, 256, 64, null, 0, null, null, 0, 0, 0.0, null, 0, 0,
+                             null, 0) == 1
     dummy = ctypes.c_void_p(0x1000)
-    assert lib.wdit_gemm_act(dummy, 64, dummy, 64, dummy, 64, 128, 100, 64, null, 0, null, null, 0, 0, 0.0, null,
-                             0) == 2  # N % 64 != 0
-    assert lib.wdit_gemm_act(dummy, 32, dummy, 64, dummy, 256, 128, 256, 64, null, 0, null, null, 0, 0, 0.0, null,
-                             0) == 2  # lda < K
+    assert lib.wdit_gemm_act(dummy, 64, dummy, 64, dummy, 64, 128, 100, 64, null, 0, null, null, 0, 0, 0.0, null, 0, 0,
+                             null, 0) == 2  # N % 64 != 0
+    assert lib.wdit_gemm_act(dummy, 32, dummy, 64, dummy, 256, 128, 256, 64, null, 0, null, null, 0, 0, 0.0, null, 0,
+                             0, null, 0) == 2  # lda < K
+    assert lib.wdit_gemm_act(dummy, 64, dummy, 64, dummy, 256, 128, 256, 64, null, 0, null, null, 0, 0, 0.0, dummy, 2,
+                             192, null, 0) == 2  # mean-square columns not a multiple of 128
     assert lib.wdit_gemm_residual(dummy, 64, dummy, 64, null, 256, dummy, 256, 128, 256, 64, null, null, null, 0, 0,
                                   null, 0, null, null, 0) == 1  # no residual
     assert lib.wdit_ln_stats(null, 0, 64, 4, 64, null, null, null, null) == 1
@@ -57,8 +60,8 @@ def test_argument_validation_without_device(lib):
 
 
 def test_norm_workspace_size(lib):
-    # fixed 64 KiB counter region, then partials M x (groups * width/256) fp32 (256-B rounded)
+    # RMSNorm partials M x (groups * width/128) fp32, 256-byte rounded
     M, groups, width = 1000, 2, 1536
-    part = ((M * groups * (width // 256) * 4 + 255) // 256) * 256
-    assert lib.wdit_gemm_norm_workspace_bytes(M, 4608, groups, width) == 64 * 1024 + part
+    part = ((M * groups * (width // 128) * 4 + 255) // 256) * 256
+    assert lib.wdit_gemm_norm_workspace_bytes(M, 4608, groups, width) == part
     assert lib.wdit_stats_tile_width() == 256

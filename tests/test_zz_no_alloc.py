@@ -39,7 +39,7 @@ def test_static_scratch_matches_workspace_entry_point(pkg):
     wq = 1.0 + rand((D,), 0.1, seed=4, dtype=torch.float32)
     wk = 1.0 + rand((D,), 0.1, seed=5, dtype=torch.float32)
     ang = rand((M, 64), 3.0, seed=6, dtype=torch.float32)
-    cos, sin = torch.cos(ang).t().contiguous(), torch.sin(ang).t().contiguous()  # pair-major [64, M]
+    cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()  # token-major [M, 64]
     stream = torch.cuda.current_stream().cuda_stream
     P = ctypes.c_void_p
 
@@ -49,14 +49,14 @@ def test_static_scratch_matches_workspace_entry_point(pkg):
     ref = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
     rc = lib.wdit_gemm_norm(P(a.data_ptr()), K, P(w.data_ptr()), K, P(ref.data_ptr()), N, M, N, K,
                             P(vec.data_ptr()), None, None, 0, 0, 0.0, 2, D, P(wq.data_ptr()), P(wk.data_ptr()),
-                            1e-6, 2, P(cos.data_ptr()), P(sin.data_ptr()), M, M, 0, P(ws.data_ptr()), need,
+                            1e-6, 2, P(cos.data_ptr()), P(sin.data_ptr()), 64, M, 0, P(ws.data_ptr()), need,
                             P(stream), 0)
     assert rc == 0
     for call in range(2):
         out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=DEV)
         rc = lib.wdit_gemm_norm_static(P(a.data_ptr()), K, P(w.data_ptr()), K, P(out.data_ptr()), N, M, N, K,
                                        P(vec.data_ptr()), None, None, 0, 0, 0.0, 2, D, P(wq.data_ptr()),
-                                       P(wk.data_ptr()), 1e-6, 2, P(cos.data_ptr()), P(sin.data_ptr()), M, M, 0,
+                                       P(wk.data_ptr()), 1e-6, 2, P(cos.data_ptr()), P(sin.data_ptr()), 64, M, 0,
                                        P(stream), 0)
         assert rc == 0, call
         torch.cuda.synchronize()
@@ -67,7 +67,7 @@ def test_static_scratch_matches_workspace_entry_point(pkg):
 def test_static_scratch_rejects_oversized_problem(pkg):
     lib = pkg._lib.load()
     assert lib.wdit_set_device(torch.cuda.current_device()) == 0
-    M, D = 200_000, 1536  # needs about 9.6 MB of partials: above the 4 MiB array
+    M, D = 200_000, 1536  # needs about 19.2 MB of partials: above the 4 MiB array
     dummy = ctypes.c_void_p(0x10000)
     rc = lib.wdit_gemm_norm_static(dummy, D, dummy, D, dummy, 3 * D, M, 3 * D, D, None, None, None, 0, 0, 0.0, 2,
                                    D, dummy, dummy, 1e-6, 0, None, None, 0, M, 0, None, 0)

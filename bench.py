@@ -212,7 +212,8 @@ def run_ours(args) -> None:
     L = seq_len()
     sp = None
     if world > 1:
-        sp = pkg.SeqParallel(dist.group.WORLD, world, rank, (LATENT[1], LATENT[2] // 2, LATENT[3] // 2), L)
+        sp = pkg.SeqParallel(dist.group.WORLD, world, rank, (LATENT[1], LATENT[2] // 2, LATENT[3] // 2), L,
+                             transport=args.transport)
     torch.manual_seed(SEED)
     params = pkg.build_wan(pkg.WAN_1_3B, seed=SEED, device=dev, num_layers=args.layers)
     model = pkg.FusedWanModel(params, sp)
@@ -311,7 +312,8 @@ def run_ours(args) -> None:
             "config": {"workload": "cfg3: Wan2.1-1.3B 30-layer DiT forward, CFG batch 2, N=32760/sample",
                        "model": "Wan2.1-1.3B (random init)", "layers": args.layers, "global_batch": BATCH,
                        "seq_len": L, "latent": list(LATENT), "context": list(TEXT), "t": T_STEP,
-                       "parallelism": f"sp{world} (token-sharded, Ulysses all-to-all)" if world > 1 else "single GPU",
+                       "parallelism": (f"sp{world} (token-sharded, Ulysses all-to-all over {args.transport})"
+                                       if world > 1 else "single GPU"),
                        "attention": "torch SDPA (out of scope)", "l2": "activations > L2 (no flush needed)"},
             "tflops": fl["total"] / (ms * 1e-3) / 1e12,
             "e2e": {"value": ms_e2e, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -334,6 +336,7 @@ def run_ours(args) -> None:
         if not args.no_cpu_baseline and world == 1:
             result["cpu_baseline"] = cpu_oracle_sample()
     if world > 1:
+        sp.close()
         dist.barrier()
         dist.destroy_process_group()
     if result is not None:
@@ -348,6 +351,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--transport", choices=("p2p", "nccl"), default="p2p",
+                    help="Ulysses all-to-all: NVLink peer stores (p2p) or NCCL all_to_all_single")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

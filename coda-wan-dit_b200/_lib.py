@@ -38,6 +38,14 @@ I = c_int
 _SIGNATURES = {
     "wdit_num_sms": (c_int, []),
     "wdit_set_cta_pair": (c_int, [I]),
+    "wdit_ipc_handle": (c_int, [P, P, ctypes.POINTER(c_longlong)]),
+    "wdit_ipc_open": (c_int, [P, ctypes.POINTER(c_void_p)]),
+    "wdit_ipc_close": (c_int, [P]),
+    "wdit_p2p_qkv_exchange": (c_int, [P, I, P, I, P, P, F, P, P, I, I, I, I, I, I, I, P, c_longlong, c_longlong,
+                                      c_uint, P, P]),
+    "wdit_p2p_out_exchange": (c_int, [P, c_longlong, c_longlong, I, I, I, I, I, I, P, c_longlong, I, c_longlong,
+                                      c_uint, P, P]),
+    "wdit_p2p_wait": (c_int, [P, I, c_uint, P]),
     "wdit_set_device": (c_int, [I]),
     "wdit_stats_tile_width": (c_int, []),
     "wdit_set_wait_limit_ns": (c_int, [c_ulonglong]),
@@ -117,7 +125,8 @@ def check(rc: int, what: str) -> None:
 _LAUNCHING = {
     "wdit_gemm_act", "wdit_gemm_residual", "wdit_gemm_norm", "wdit_ln_stats", "wdit_fold_weight",
     "wdit_layernorm_modulation", "wdit_rmsnorm", "wdit_qk_rms_rope_from_partials", "wdit_rope_table",
-    "wdit_block_mean_sq", "wdit_ulysses_pack", "wdit_seq_gather", "wdit_seq_scatter", "wdit_ulysses_unpack",
+    "wdit_ulysses_pack", "wdit_seq_gather", "wdit_seq_scatter", "wdit_ulysses_unpack",
+    "wdit_p2p_qkv_exchange", "wdit_p2p_out_exchange", "wdit_p2p_wait",
 }
 launch_counter = {"n": 0}
 

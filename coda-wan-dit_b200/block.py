@@ -245,17 +245,27 @@ class FusedWanBlock(nn.Module):
 
         # --- self-attention branch ---
         qkv = torch.empty((M, 3 * D), dtype=torch.bfloat16, device=dev)
+        # With the NVLink peer-store exchange the q/k RMSNorm + RoPE happen inside the exchange
+        # kernel: the GEMM only emits the raw projection and its mean-square partials.
+        fused_exchange = sp is not None and sp.fuses_qk_norm
+        part = torch.empty((M, 2 * D // ops.RMS_BLOCK), dtype=torch.float32, device=dev) if fused_exchange else None
         for b in range(Be):
             r0, r1 = (0, M) if Be == 1 else (b * L, (b + 1) * L)
             wf, cs, vec = ops.fold_weight(self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=e_row(b, 1),
                                           shift_a=mod[0], shift_b=e_row(b, 0), bias=self.b_qkv)
+            ln = ops.LnFold(cs, stats[r0:r1], self.eps)
+            if fused_exchange:
+                ops.gemm_act(xb[r0:r1], wf, vec=vec, ln=ln, out=qkv[r0:r1], ms_out=part[r0:r1], ms_cols=2 * D)
+                continue
             ops.gemm_norm(
-                xb[r0:r1], wf, vec=vec, ln=ops.LnFold(cs, stats[r0:r1], self.eps), norm_groups=2, norm_width=D,
+                xb[r0:r1], wf, vec=vec, ln=ln, norm_groups=2, norm_width=D,
                 norm_w=(self.w_nq, self.w_nk), norm_eps=self.rms_eps, rope_groups=2, rope_cos=cos, rope_sin=sin,
                 rows_per_batch=grid_rows_per_batch, token_offset=token_offset, out=qkv[r0:r1],
                 workspace=self.workspace,
             )
-        if sp is not None:
+        if fused_exchange:
+            y = sp.self_attention_p2p(qkv, part, self.w_nq, self.w_nk, self.rms_eps, cos, sin, B, L, H, hd)
+        elif sp is not None:
             y = sp.self_attention(qkv, B, L, H, hd)
         else:
             q = qkv[:, :D].view(B, L, H, hd)

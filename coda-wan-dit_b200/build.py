@@ -18,7 +18,7 @@ PKG_DIR = Path(__file__).resolve().parent
 ROOT = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libwdit.so"
-SOURCES = ["gemm.cu", "aux.cu", "comm.cu"]
+SOURCES = ["gemm.cu", "aux.cu", "comm.cu", "p2p.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

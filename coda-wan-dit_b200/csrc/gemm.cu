@@ -708,6 +708,9 @@ int num_sms() {
 
 // Whether the tensor-bound variants (bias/GELU, long-K residual) run on CTA pairs.
 int g_cta_pair = 1;
+unsigned long long g_wait_limit_host = 2000000000ull;  // host copy of g_wdit_wait_limit_ns
+std::mutex g_err_ptr_mutex;
+unsigned int* g_err_ptr[64] = {};
 
 template <int KIND, bool PAIR>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const CUtensorMap& c,
@@ -872,6 +875,25 @@ int run_norm(const void* A, int lda, const void* B, int ldb, void* out, int ldo,
 }
 
 }  // namespace
+
+int error_record_ptr(unsigned int** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+  if (dev < 0 || dev >= 64) return WDIT_ERR_ARG;
+  std::lock_guard<std::mutex> lock(g_err_ptr_mutex);
+  if (g_err_ptr[dev] == nullptr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_wdit_error);
+    if (e != cudaSuccess) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+    g_err_ptr[dev] = static_cast<unsigned int*>(addr);
+  }
+  *out = g_err_ptr[dev];
+  return WDIT_OK;
+}
+
+unsigned long long wait_limit_ns() { return g_wait_limit_host; }
+
 }  // namespace wdit
 
 using namespace wdit;
@@ -890,6 +912,7 @@ int wdit_set_cta_pair(int enable) {
 
 int wdit_set_wait_limit_ns(unsigned long long ns) {
   cudaError_t e = cudaMemcpyToSymbol(g_wdit_wait_limit_ns, &ns, sizeof(ns));
+  if (e == cudaSuccess) g_wait_limit_host = ns;
   return e == cudaSuccess ? WDIT_OK : WDIT_ERR_CUDA_BASE + static_cast<int>(e);
 }
 

@@ -47,4 +47,9 @@ int launch_rms_rope_apply(void* x, int ldx, int M, const float* part, int part_l
                           const float* w0, const float* w1, float eps, int rope_groups, const float* rope_cos,
                           const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream);
 
+// Device address of the library's error record {code, site, block, extra} on the current
+// device (defined with the GEMM kernels), and the host copy of the device-side wait limit.
+int error_record_ptr(unsigned int** out);
+unsigned long long wait_limit_ns();
+
 }  // namespace wdit

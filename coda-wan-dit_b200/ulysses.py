@@ -7,23 +7,102 @@ dealt out as units (U = B*H/P per rank; Wan-1.3B's 12 heads x CFG batch 2 = 24 u
 evenly over 8 ranks), regrouped with one all-to-all before attention and one after.
 Cross-attention needs no exchange (the 512-token context is replicated).
 
-Layout kernels (wdit_ulysses_pack / seq_gather / seq_scatter / ulysses_unpack) move the
-rows into contiguous per-peer blocks; torch.distributed.all_to_all_single (NCCL over
-NVLink / NVSwitch) moves the blocks.
+Two transports:
+
+* "p2p" (default): every rank maps its peers' exchange regions once (CUDA IPC) and the
+  exchanges are single kernels that store straight into peer memory over NVLink
+  (wdit_p2p_qkv_exchange also applies the q/k RMSNorm + RoPE, so the QKV GEMM skips its own
+  RMSNorm/RoPE pass), each followed by a bounded stream-ordered wait for all ranks' arrival
+  flags (wdit_p2p_wait).
+* "nccl": layout kernels (wdit_ulysses_pack / seq_gather / seq_scatter / ulysses_unpack) move
+  the rows into contiguous per-peer blocks and torch.distributed.all_to_all_single (NCCL over
+  NVLink / NVSwitch) moves the blocks.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from . import _lib
 from ._lib import call, ptr, stream_ptr
+
+_HANDLE_BYTES = 64
+
+
+def _round256(n: int) -> int:
+    return (n + 255) // 256 * 256
+
+
+class _Exchange:
+    """One rank's exchange region (mapped into every peer) for one (B, Lp, H, hd) shape."""
+
+    def __init__(self, sp: "SeqParallel", B: int, Lp: int, H: int, hd: int, device):
+        P, r = sp.world, sp.rank
+        self.shape = (B, Lp, H, hd)
+        U, L, D = B * H // P, P * Lp, H * hd
+        self.full_bytes = 3 * U * L * hd * 2
+        self.y_bytes = B * Lp * D * 2
+        fr, yr = _round256(self.full_bytes), _round256(self.y_bytes)
+        self.full_off = (0, fr)
+        self.y_off = (2 * fr, 2 * fr + yr)
+        self.flag_off = (2 * fr + 2 * yr, 2 * fr + 2 * yr + _round256(4 * P))
+        total = self.flag_off[1] + _round256(4 * P)
+        self.region = torch.empty(total, dtype=torch.uint8, device=device)
+        self.region[self.flag_off[0]:].zero_()
+        self.done = torch.zeros(2, dtype=torch.int32, device=device)
+        lib = _lib.load()
+        handle = ctypes.create_string_buffer(_HANDLE_BYTES)
+        off = ctypes.c_longlong(0)
+        call("wdit_ipc_handle", ptr(self.region), handle, ctypes.byref(off))
+        mine = torch.tensor(list(handle.raw) + list(int(off.value).to_bytes(8, "little")), dtype=torch.uint8,
+                            device=device)
+        every = torch.empty((P, mine.numel()), dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, mine, group=sp.group)
+        every = every.cpu()
+        self.opened: list[int] = []
+        bases = []
+        for p in range(P):
+            if p == r:
+                bases.append(ptr(self.region))
+                continue
+            raw = bytes(every[p, :_HANDLE_BYTES].tolist())
+            peer_off = int.from_bytes(bytes(every[p, _HANDLE_BYTES:].tolist()), "little")
+            base = ctypes.c_void_p(0)
+            call("wdit_ipc_open", ctypes.create_string_buffer(raw, _HANDLE_BYTES), ctypes.byref(base))
+            self.opened.append(int(base.value))
+            bases.append(int(base.value) + peer_off)
+        self.peers = (ctypes.c_void_p * P)(*bases)
+        self._lib = lib
+        torch.cuda.synchronize(device)
+        dist.barrier(group=sp.group)  # every region mapped and its flags zeroed before any write
+
+    def flags(self, x: int) -> int:
+        return ptr(self.region) + self.flag_off[x]
+
+    def full(self, buf: int, U: int, L: int, hd: int) -> torch.Tensor:
+        o = self.full_off[buf]
+        return self.region[o:o + self.full_bytes].view(torch.bfloat16).view(3, U, L, hd)
+
+    def y(self, buf: int, rows: int, D: int) -> torch.Tensor:
+        o = self.y_off[buf]
+        return self.region[o:o + self.y_bytes].view(torch.bfloat16).view(rows, D)
+
+    def close(self) -> None:
+        for base in self.opened:
+            self._lib.wdit_ipc_close(ctypes.c_void_p(base))
+        self.opened = []
 
 
 class SeqParallel:
-    def __init__(self, group, world: int, rank: int, grid: tuple[int, int, int], seq_len: int):
+    def __init__(self, group, world: int, rank: int, grid: tuple[int, int, int], seq_len: int,
+                 transport: str = "p2p"):
         if seq_len % world != 0:
             raise ValueError(f"sequence length {seq_len} is not divisible by {world} ranks")
+        if transport not in ("p2p", "nccl"):
+            raise ValueError(f"unknown transport {transport!r} (p2p or nccl)")
         self.group = group
         self.world = world
         self.rank = rank
@@ -31,6 +110,51 @@ class SeqParallel:
         self.seq_len = seq_len
         self.local_len = seq_len // world
         self.token_offset = rank * self.local_len
+        self.transport = transport
+        self._x: _Exchange | None = None
+        self.epoch = 0
+
+    @property
+    def fuses_qk_norm(self) -> bool:
+        """True when self_attention_p2p takes the raw QKV GEMM output and its RMSNorm partials."""
+        return self.transport == "p2p"
+
+    def close(self) -> None:
+        """Unmap the peers' exchange regions (call on every rank before destroying the group)."""
+        if self._x is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)  # no rank still writes into a region being unmapped
+            self._x.close()
+            self._x = None
+
+    def self_attention_p2p(self, qkv: torch.Tensor, part: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
+                           eps: float, cos: torch.Tensor, sin: torch.Tensor, B: int, Lp: int, H: int,
+                           hd: int) -> torch.Tensor:
+        """qkv [B*Lp, 3*H*hd] raw QKV GEMM output of this rank's tokens, part [B*Lp, 2*H] its q/k
+        mean-square partials -> attention output [B*Lp, H*hd] for the same tokens."""
+        P = self.world
+        assert Lp == self.local_len and (B * H) % P == 0 and hd == 128
+        assert qkv.stride(1) == 1 and part.stride(1) == 1 and cos.stride(1) == 1 and sin.stride() == cos.stride()
+        if self._x is None or self._x.shape != (B, Lp, H, hd):
+            if self._x is not None:
+                self.close()
+            self._x = _Exchange(self, B, Lp, H, hd, qkv.device)
+        x = self._x
+        U, L, D = B * H // P, P * Lp, H * hd
+        self.epoch += 1
+        e, buf = self.epoch, self.epoch & 1
+        st = stream_ptr()
+        call("wdit_p2p_qkv_exchange", ptr(qkv), qkv.stride(0), ptr(part), part.stride(0), ptr(wq), ptr(wk),
+             float(eps), ptr(cos), ptr(sin), cos.stride(0), B, Lp, H, hd, P, self.rank, x.peers,
+             x.full_off[buf], x.flag_off[0], e, ptr(x.done), st)
+        call("wdit_p2p_wait", x.flags(0), P, e, st)
+        full = x.full(buf, U, L, hd)
+        o = F.scaled_dot_product_attention(full[0].unsqueeze(0), full[1].unsqueeze(0), full[2].unsqueeze(0))[0]
+        assert o.stride(2) == 1
+        call("wdit_p2p_out_exchange", ptr(o), o.stride(0), o.stride(1), B, Lp, H, hd, P, self.rank, x.peers,
+             x.y_off[buf], D, x.flag_off[1], e, ptr(x.done) + 4, st)
+        call("wdit_p2p_wait", x.flags(1), P, e, st)
+        return x.y(buf, B * Lp, D)
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor) -> None:
         if self.world == 1:

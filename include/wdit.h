@@ -225,6 +225,43 @@ int wdit_seq_scatter(const void* o, long long unit_stride, long long tok_stride,
 /* dst rows (b*Lp + t), columns h*hd + i <- recv[P][U][Lp][hd]. */
 int wdit_ulysses_unpack(const void* recv, int B, int Lp, int H, int hd, int P, void* dst, int ld, void* stream);
 
+/* ---- the same all-to-all as direct NVLink stores into peer GPUs' memory (no reference
+ * counterpart). Each rank exposes an exchange region of its own memory (256-byte aligned):
+ *   full[2][3][U][L][hd] bf16 at full_off[buf], y[2][B*Lp][ldy] bf16 at y_off[buf],
+ *   flags[2][P] u32 at flag_off[x] (zero before first use)
+ * mapped into every peer with CUDA IPC; peer_bases[p] = rank p's region as mapped in the
+ * calling process (its own region for p == rank). `epoch` counts exchanges from 1 and picks
+ * buffer epoch & 1. Each exchange kernel finishes by publishing epoch into flags[x][rank] of
+ * every rank (system-scope release); wdit_p2p_wait blocks the stream until all P ranks have
+ * published it (bounded by the wait limit; on expiry the error record holds {0x7117, 9,
+ * missing rank, epoch}). done_ctr: one zeroed u32 per exchange kernel, private to the rank. */
+
+/* 64-byte IPC handle of the allocation holding ptr, and ptr's offset inside it. */
+int wdit_ipc_handle(const void* ptr, void* handle_out, long long* offset_out);
+/* Map a peer's allocation (peer access enabled lazily); base of the mapping. */
+int wdit_ipc_open(const void* handle, void** base_out);
+int wdit_ipc_close(void* base);
+
+/* Exchange 1: qkv[B*Lp, >= 3*H*hd] (QKV GEMM output, q and k not yet normalized), part[B*Lp,
+ * part_ld] (its per-128-column mean squares, q blocks then k blocks), q/k RMSNorm weights,
+ * token-major RoPE tables indexed by global token (rank*Lp + t). Writes RMSNorm + RoPE(q, k)
+ * and v of every head into full[epoch & 1] of the rank owning its unit. hd = 128. */
+int wdit_p2p_qkv_exchange(const void* qkv, int ldq, const float* part, int part_ld, const float* wq,
+                          const float* wk, float eps, const float* rope_cos, const float* rope_sin, int rope_ld,
+                          int B, int Lp, int H, int hd, int P, int rank, const void* const* peer_bases,
+                          long long full_off, long long flag_off, unsigned int epoch, unsigned int* done_ctr,
+                          void* stream);
+
+/* Exchange 2: attention output o[j*o_unit_stride + g*o_tok_stride + i] of this rank's units
+ * (j < U, global token g < P*Lp) -> y[epoch & 1] rows (b*Lp + t), columns h*hd + i of the rank
+ * owning token g. */
+int wdit_p2p_out_exchange(const void* o, long long o_unit_stride, long long o_tok_stride, int B, int Lp, int H,
+                          int hd, int P, int rank, const void* const* peer_bases, long long y_off, int ldy,
+                          long long flag_off, unsigned int epoch, unsigned int* done_ctr, void* stream);
+
+/* Stream-ordered bounded wait until flags[0..P) (this rank's flags of one exchange) reach epoch. */
+int wdit_p2p_wait(const unsigned int* flags, int P, unsigned int epoch, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

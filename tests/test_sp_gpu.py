@@ -27,7 +27,7 @@ def _inputs(cfg, dev):
     return wan_ref.model_inputs(cfg, LATENT, 2, seed=5, device=dev)
 
 
-def _worker(rank, world, port, root, ret):
+def _worker(rank, world, port, root, transport, ret):
     import sys
     from datetime import timedelta
 
@@ -46,19 +46,24 @@ def _worker(rank, world, port, root, ret):
         cfg = wan_ref.WAN_1_3B
         inp = _inputs(cfg, dev)
         L = inp["seq_len"]
-        sp = pkg.SeqParallel(dist.group.WORLD, world, rank, (LATENT[0], LATENT[1] // 2, LATENT[2] // 2), L)
+        sp = pkg.SeqParallel(dist.group.WORLD, world, rank, (LATENT[0], LATENT[1] // 2, LATENT[2] // 2), L,
+                             transport=transport)
         params = pkg.build_wan(pkg.WAN_1_3B, seed=11, device=dev, num_layers=LAYERS)
+        model = pkg.FusedWanModel(params, sp)
         with torch.no_grad():
-            y = pkg.FusedWanModel(params, sp)(inp["x"], inp["t"], inp["context"], L)
+            y = model(inp["x"], inp["t"], inp["context"], L)
+            y2 = model(inp["x"], inp["t"], inp["context"], L)  # second forward: the other exchange buffers
         torch.cuda.synchronize()
         pkg._lib.raise_on_device_error()
-        ret[rank] = y.float().cpu()
+        ret[rank] = (y.float().cpu(), y2.float().cpu())
+        sp.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_sequence_parallel_matches_single_gpu(pkg):
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
+def test_sequence_parallel_matches_single_gpu(pkg, transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from pathlib import Path
@@ -74,10 +79,11 @@ def test_sequence_parallel_matches_single_gpu(pkg):
     with torch.no_grad():
         full = pkg.FusedWanModel(params)(inp["x"], inp["t"], inp["context"], L, return_tokens=True).float().cpu()
     ret = mp.Manager().dict()
-    mp.start_processes(_worker, args=(2, _port(), root, ret), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(2, _port(), root, transport, ret), nprocs=2, start_method="spawn", join=True)
     Lp = L // 2
     for r in range(2):
         want = full[:, r * Lp:(r + 1) * Lp]
-        got = ret[r]
+        got, got2 = ret[r]
         rel = ((got - want).norm() / want.norm()).item()
         assert rel < 1e-2, (r, rel)
+        assert torch.equal(got, got2), r  # deterministic across epochs / buffers

@@ -84,7 +84,7 @@ def traffic_from_profiles(kernel: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms during the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -94,16 +94,30 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.path = None
+        self.skip = 0
+
+    def _lines(self) -> list[str]:
+        try:
+            return [ln for ln in Path(self.path).read_text().splitlines() if ln.count(",") >= 8]
+        except OSError:
+            return []
 
     def start(self):
+        """Start sampling every 50 ms; returns once sampling is live, so that only samples taken
+        after this call (inside the timed region that follows) are kept."""
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 10.0 and not self._lines():
+            time.sleep(0.02)
+        self.skip = len(self._lines())
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -114,7 +128,7 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         rows = []
-        for line in Path(self.path).read_text().splitlines():
+        for line in self._lines()[self.skip:]:
             f = [x.strip() for x in line.split(",")]
             if len(f) >= 9:
                 rows.append(f)

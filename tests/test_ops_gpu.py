@@ -113,8 +113,9 @@ def test_gemm_act_cta_pair(pkg, M, N, K):
     assert rel_l2(got2, got1) < 1e-3
 
 
-@pytest.mark.parametrize("M,N,K", [(300, 1536, 4096), (4095, 1536, 8960), (32760, 1536, 8960)])
-def test_gemm_residual_long_k_cta_pair(pkg, M, N, K):
+@pytest.mark.parametrize("M,N,K", [(300, 1536, 4096), (4095, 1536, 8960), (32760, 1536, 8960), (300, 512, 256),
+                                   (4095, 1536, 1536), (32760, 1536, 1536)])
+def test_gemm_residual_cta_pair(pkg, M, N, K):
     a = rand((M, K), seed=33)
     w = rand((N, K), 0.02, seed=34)
     c = rand((M, N), 1.0, seed=35, dtype=torch.float32)

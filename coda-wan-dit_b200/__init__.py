@@ -5,7 +5,7 @@ Import name: ``coda_wan_dit_b200`` (the directory name has hyphens; load it with
 ``load_package()`` from the repository root helpers, or add the directory's parent to
 ``sys.path`` and register it under that name).
 """
-from . import _lib, ops  # noqa: F401
+from . import _lib, ops, sampler  # noqa: F401
 from .block import Carry, CodaFullBlock, FusedWanBlock  # noqa: F401
 from .model import WAN_14B, WAN_1_3B, FusedWanModel, WanParams, WanShape, build_wan  # noqa: F401
 from .ulysses import SeqParallel  # noqa: F401
@@ -22,4 +22,5 @@ __all__ = [
     "WAN_14B",
     "build_wan",
     "SeqParallel",
+    "sampler",
 ]

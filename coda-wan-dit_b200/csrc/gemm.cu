@@ -88,16 +88,19 @@ template <>
 struct Cfg<kEpiResidual> {
   static constexpr int kStages = 3;
   static constexpr int kPairStages = 0;  // HBM-bound: the pair buys nothing
-  static constexpr int kNumCBuf = 4;
-  static constexpr int kLookahead = 2;
+  static constexpr int kHalves = 2;      // both column halves' warps work (latency-bound epilogue)
+  static constexpr int kNumCBuf = 4;     // 2 per half
+  static constexpr int kLookahead = 1;   // per half
   static constexpr bool kXStaged = true;  // bf16 copy staged (64-byte swizzle) + TMA store
-  static constexpr uint32_t kEpiBytes = kNumCBuf * 16384 + 2 * kStgBytes;
-  static constexpr int kEpiArrivals = kEpiThreads;
+  // ring + one staging tile per half + the halves' row-statistics exchange (128 x 3 floats)
+  static constexpr uint32_t kEpiBytes = kNumCBuf * 16384 + 2 * kStgBytes + 128 * 3 * 4;
+  static constexpr int kEpiArrivals = kHalves * kEpiThreads;
 };
 template <>
 struct Cfg<kEpiResidualLongK> {
   static constexpr int kStages = 4;
   static constexpr int kPairStages = 6;
+  static constexpr int kHalves = 1;
   static constexpr int kNumCBuf = 2;
   static constexpr int kLookahead = 1;
   static constexpr bool kXStaged = false;  // bf16 copy stored from registers
@@ -114,8 +117,9 @@ constexpr uint32_t smem_bytes() {
   return 1024 /*alignment slack*/ + num_stages<KIND, PAIR>() * (PAIR ? kPairStageBytes : kStageBytes) +
          Cfg<KIND>::kEpiBytes + 256 /*barriers + tmem slot*/;
 }
-static_assert(smem_bytes<kEpiAct, true>() <= 232448 && smem_bytes<kEpiResidualLongK, true>() <= 232448,
-              "pair configurations exceed the 227 KB shared-memory limit");
+static_assert(smem_bytes<kEpiAct, true>() <= 232448 && smem_bytes<kEpiResidualLongK, true>() <= 232448 &&
+                  smem_bytes<kEpiResidual, false>() <= 232448,
+              "configuration exceeds the 227 KB shared-memory limit");
 
 // ---------------------------------------------------------------------------
 // Epilogue helpers
@@ -465,36 +469,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (lane == 0) bulk_wait_all<0>();
-    } else if (half == 0) {
+    } else if (half < Cfg<KIND>::kHalves) {
       // ----------------------------- residual -----------------------------
-      const int et = ht;
-      constexpr int NB = Cfg<KIND>::kNumCBuf;
-      constexpr int LA = Cfg<KIND>::kLookahead;
-      static_assert(LA >= 1 && LA < NB, "lookahead must leave one buffer being stored");
+      // kHalves = 1: warps 2-5 process the tile's eight 32-column chunks in turn.
+      // kHalves = 2: half h (warps 2-5 / 6-9) processes chunks h, h + 2, h + 4, h + 6; each half
+      // owns every other residual buffer and one bf16 staging buffer, issues its own loads and
+      // stores, and the halves merge their row statistics through shared memory per tile.
+      constexpr int HV = Cfg<KIND>::kHalves;
+      const int et = ht;          // thread index inside the half
+      const bool lead = et == 0;  // issues this half's TMA loads and stores
+      constexpr int NB = Cfg<KIND>::kNumCBuf;  // residual buffers in all
+      constexpr int NBH = NB / HV;             // ... per half
+      constexpr int LA = Cfg<KIND>::kLookahead;  // chunks requested ahead, per half
+      static_assert(LA >= 1 && LA < NBH, "lookahead must leave one buffer being stored");
       constexpr int CPT = BN / 32;  // 32-column chunks per tile
+      constexpr int CPH = CPT / HV;  // ... per half
       constexpr bool XS = Cfg<KIND>::kXStaged;
+      static_assert(HV == 1 || !XS || NBH - LA - 1 == 0, "one staging buffer per half needs drained stores");
       uint8_t* cbuf0 = epi_base;
       uint8_t* xbuf0 = epi_base + NB * 16384;
+      float* st_x = reinterpret_cast<float*>(epi_base + NB * 16384 + (XS ? 2 * kStgBytes : 0u));  // [128][3]
       const int my_tiles = (t_first < s.tiles) ? (s.tiles - 1 - t_first) / t_step + 1 : 0;
-      const int total_chunks = my_tiles * CPT;
+      const int total_k = my_tiles * CPH;
       const bool has_x = p.has_x_map;
-      // Chunk g -> (tile, column chunk); issue the residual load of chunk g.
-      auto issue_load = [&](int g) {
-        const int ti = g / CPT;
-        const int c = g - ti * CPT;
+      auto buf_of = [&](int k) { return half + HV * (k % NBH); };
+      // This half's k-th chunk -> (tile, column chunk); issue its residual load.
+      auto issue_load = [&](int k) {
+        const int ti = k / CPH;
+        const int c = half + HV * (k - ti * CPH);
         int m_blk, n_blk;
         tile_coords(t_first + ti * t_step, m_blk, n_blk);
         const int n0 = n_blk * BN + c * 32;
-        uint64_t* bar = &cload_bar[g % NB];
+        const int bi = buf_of(k);
+        uint64_t* bar = &cload_bar[bi];
         mbar_arrive_expect_tx(bar, 16384);
-        tma_load_2d(cbuf0 + (g % NB) * 16384, &tmC, bar, n0 < s.N ? n0 : 0, m_blk * BM);
+        tma_load_2d(cbuf0 + bi * 16384, &tmC, bar, n0 < s.N ? n0 : 0, m_blk * BM);
       };
-      if (et == 0) {
-        for (int g = 0; g < LA && g < total_chunks; ++g) issue_load(g);
+      if (lead) {
+        for (int k = 0; k < LA && k < total_k; ++k) issue_load(k);
       }
-      int g = 0;
+      int k = 0;
       bool failed = false;
-      for (int ti = 0; ti < my_tiles && !failed; ++ti) {
+      for (int ti = 0; ti < my_tiles; ++ti) {
         int m_blk, n_blk;
         tile_coords(t_first + ti * t_step, m_blk, n_blk);
         const bool rows_any = m_blk * BM < s.M;  // false only for a pair's trailing half
@@ -502,7 +518,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tphase = (ti >> 1) & 1;
         {
           const bool ok = wait_parity<PAIR>(&tfull_bar[buf], tphase, kSiteEpiTmemFull);
-          if (named_bar_any(2, kEpiThreads, !ok)) break;
+          if (named_bar_any(3, HV * kEpiThreads, !ok)) {
+            failed = true;
+            break;
+          }
         }
         tc_fence_after();
         const int row = m_blk * BM + r;
@@ -510,22 +529,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* gb = p.gate_b != nullptr ? p.gate_b + static_cast<size_t>(batch) * p.gate_b_stride : nullptr;
         float run_n = 0.f, run_mean = 0.f, run_m2 = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < CPT; ++c, ++g) {
+        for (int j = 0; j < CPH; ++j, ++k) {
+          const int c = half + HV * j;
           const int n0 = n_blk * BN + c * 32;
-          if (et == 0) {
-            // Buffer of chunk g+LA last held chunk g+LA-NB: its store must have been read.
-            bulk_wait_read<NB - LA - 1>();
-            if (g + LA < total_chunks) issue_load(g + LA);
+          const int bi = buf_of(k);
+          const int xs = HV == 1 ? (k & 1) : half;  // bf16 staging buffer of this chunk
+          if (lead) {
+            // The buffer of chunk k + LA last held chunk k + LA - NBH: its store must have been read.
+            bulk_wait_read<NBH - LA - 1>();
+            if (k + LA < total_k) issue_load(k + LA);
           }
-          named_bar_sync(1, kEpiThreads);
+          named_bar_sync(1 + half, kEpiThreads);
           float acc[32];
           tmem_ld32(tmem_base + lane_off + buf * BN + c * 32, acc);
-          if (c == CPT - 1) {
+          if (j == CPH - 1) {
             release_acc(buf);
           }
-          const bool c_ok = wait_parity(&cload_bar[g % NB], (g / NB) & 1, kSiteEpiCLoad);
+          const bool c_ok = wait_parity(&cload_bar[bi], (k / NBH) & 1, kSiteEpiCLoad);
           const bool col_ok = n0 < s.N;
-          const uint32_t crow = smem_u32(cbuf0 + (g % NB) * 16384) + r * 128;
+          const uint32_t crow = smem_u32(cbuf0 + bi * 16384) + r * 128;
           float out[32];
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
@@ -550,10 +572,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                   gg[0] += u.x; gg[1] += u.y; gg[2] += u.z; gg[3] += u.w;
                 }
 #pragma unroll
-                for (int j = 0; j < 4; ++j) out[4 * q + j] = fmaf(acc[4 * q + j] + bb[j], gg[j], out[4 * q + j]);
+                for (int i = 0; i < 4; ++i) out[4 * q + i] = fmaf(acc[4 * q + i] + bb[i], gg[i], out[4 * q + i]);
               } else {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) out[4 * q + j] += acc[4 * q + j] + bb[j];
+                for (int i = 0; i < 4; ++i) out[4 * q + i] += acc[4 * q + i] + bb[i];
               }
             }
           }
@@ -568,13 +590,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             // independent accumulators keep the dependency chains short.
             float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int j = 0; j < 32; ++j) s4[j & 3] += out[j];
+            for (int i = 0; i < 32; ++i) s4[i & 3] += out[i];
             const float cmean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / 32.f);
             float m4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float d = out[j] - cmean;
-              m4[j & 3] = fmaf(d, d, m4[j & 3]);
+            for (int i = 0; i < 32; ++i) {
+              const float d = out[i] - cmean;
+              m4[i & 3] = fmaf(d, d, m4[i & 3]);
             }
             const float cm2 = (m4[0] + m4[1]) + (m4[2] + m4[3]);
             const float tot = run_n + 32.f;
@@ -584,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             run_n = tot;
           }
           if (XS && has_x) {
-            const uint32_t xrow = smem_u32(xbuf0 + (g & 1) * kStgBytes) + r * 64;
+            const uint32_t xrow = smem_u32(xbuf0 + xs * kStgBytes) + r * 64;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               st_shared_v4(xrow + ((q ^ ((r >> 1) & 3)) << 4), pack_bf16x2(out[8 * q], out[8 * q + 1]),
@@ -602,28 +624,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           fence_proxy_async_smem();
-          if (named_bar_any(1, kEpiThreads, !c_ok)) {
-            failed = true;
-            break;
-          }
-          if (et == 0) {
-            if (col_ok && rows_any) {
-              tma_store_2d(&tmOut, cbuf0 + (g % NB) * 16384, n0, m_blk * BM);
-              if (XS && has_x) tma_store_2d(&tmX, xbuf0 + (g & 1) * kStgBytes, n0, m_blk * BM);
+          // A residual load that did not arrive fails the chunk; the halves decide together at
+          // the end of the tile (no early exit here, so both halves keep meeting the same barriers).
+          if (named_bar_any(1 + half, kEpiThreads, !c_ok)) failed = true;
+          if (lead) {
+            if (col_ok && rows_any && !failed) {
+              tma_store_2d(&tmOut, cbuf0 + bi * 16384, n0, m_blk * BM);
+              if (XS && has_x) tma_store_2d(&tmX, xbuf0 + xs * kStgBytes, n0, m_blk * BM);
             }
             bulk_commit();
           }
         }
-        if (!failed && p.stats_out != nullptr && row < s.M) {
+        if (HV == 2 && half == 1 && p.stats_out != nullptr) {
+          st_x[3 * r] = run_n;
+          st_x[3 * r + 1] = run_mean;
+          st_x[3 * r + 2] = run_m2;
+        }
+        if (named_bar_any(3, HV * kEpiThreads, failed)) {
+          failed = true;
+          break;
+        }
+        if (half == 0 && p.stats_out != nullptr && row < s.M) {
+          if (HV == 2) {
+            // Chan merge with the other half's statistics of the same row.
+            const float n1 = st_x[3 * r];
+            if (n1 > 0.f) {
+              const float tot = run_n + n1;
+              const float delta = st_x[3 * r + 1] - run_mean;
+              run_mean += delta * (n1 / tot);
+              run_m2 += st_x[3 * r + 2] + delta * delta * (run_n * n1 / tot);
+              run_n = tot;
+            }
+          }
           const int ntiles = (s.N + BN - 1) / BN;
           *reinterpret_cast<float2*>(p.stats_out + (static_cast<size_t>(row) * ntiles + n_blk) * 2) =
               make_float2(run_mean, run_m2);
         }
       }
-      if (et == 0) bulk_wait_all<0>();
+      if (lead) bulk_wait_all<0>();
       // Do not leave with residual loads in flight (only reachable after a failure).
-      if (failed && et == 0) {
-        for (int gg = g; gg <= g + LA && gg < total_chunks; ++gg) wait_parity(&cload_bar[gg % NB], (gg / NB) & 1, kSiteDrain);
+      if (failed && lead) {
+        for (int kk = k; kk < k + LA && kk < total_k; ++kk) {
+          wait_parity(&cload_bar[buf_of(kk)], (kk / NBH) & 1, kSiteDrain);
+        }
       }
     }
   }

@@ -218,17 +218,35 @@ class FusedWanModel(nn.Module):
                              persistent=False)
 
     # -- embeddings --------------------------------------------------------
-    def embed_tokens(self, x_list, seq_len):
-        """Patch embedding -> [B, seq_len, dim] bf16 (zero-padded), grids, true lengths."""
+    def embed_tokens(self, x_list, seq_len, token_range: tuple[int, int] | None = None):
+        """Patch embedding -> [B, seq_len, dim] bf16 (zero-padded), grids, true lengths.
+
+        token_range (lo, hi): embed only tokens [lo, hi) of every sample (a token shard); only the
+        latent frames that hold them go through the convolution."""
         pe = self.model.patch_embedding
         w = pe.weight.to(torch.bfloat16)
         b = pe.bias.to(torch.bfloat16)
-        xs = [F.conv3d(u.unsqueeze(0).to(torch.bfloat16), w, b, stride=self.patch) for u in x_list]
-        grids = [tuple(int(v) for v in u.shape[2:]) for u in xs]
-        xs = [u.flatten(2).transpose(1, 2) for u in xs]
-        lens = [u.shape[1] for u in xs]
-        x = torch.cat([F.pad(u, (0, 0, 0, seq_len - u.shape[1])) for u in xs])
-        return x, grids, lens
+        pt, ph, pw = self.patch
+        grids, lens, xs = [], [], []
+        for u in x_list:
+            g = (u.shape[1] // pt, u.shape[2] // ph, u.shape[3] // pw)
+            grids.append(g)
+            lens.append(g[0] * g[1] * g[2])
+            if token_range is None:
+                v = F.conv3d(u.unsqueeze(0).to(torch.bfloat16), w, b, stride=self.patch)
+                xs.append(F.pad(v.flatten(2).transpose(1, 2), (0, 0, 0, seq_len - lens[-1])))
+                continue
+            lo, hi = token_range
+            per_frame = g[1] * g[2]
+            f0 = min(lo // per_frame, g[0])
+            f1 = min(-(-hi // per_frame), g[0])
+            if f1 > f0:
+                v = F.conv3d(u[:, f0 * pt:f1 * pt].unsqueeze(0).to(torch.bfloat16), w, b, stride=self.patch)
+                v = v.flatten(2).transpose(1, 2)[:, lo - f0 * per_frame:hi - f0 * per_frame]
+            else:
+                v = torch.zeros((1, 0, self.dim), dtype=torch.bfloat16, device=u.device)
+            xs.append(F.pad(v, (0, 0, 0, (hi - lo) - v.shape[1])))  # tokens past the sample's end are zero
+        return torch.cat(xs), grids, lens
 
     def embed_time(self, t: torch.Tensor):
         e = self.model.time_embedding(sinusoidal_embedding(self.freq_dim, t).float())
@@ -279,13 +297,11 @@ class FusedWanModel(nn.Module):
         tv = t.tolist()
         shared_e = all(v == tv[0] for v in tv)
         t = t.to(dev)
-        x, grids, lens = self.embed_tokens(x_list, seq_len)
+        sp = self.sp
+        token_range = None if sp is None else (sp.token_offset, sp.token_offset + sp.local_len)
+        x, grids, lens = self.embed_tokens(x_list, seq_len, token_range)
         e, e0 = self.embed_time(t[:1] if shared_e else t)
         context = self.embed_text(context_list, text_len)
-        sp = self.sp
-        if sp is not None:
-            Lp = sp.local_len
-            x = x[:, sp.token_offset:sp.token_offset + Lp]
         Lx = x.shape[1]
         seq_lens = torch.tensor(lens, dtype=torch.long) if sp is None else None
         grid_sizes = torch.tensor(grids, dtype=torch.long)

@@ -200,8 +200,10 @@ def run_reference(args) -> None:
         "metric": METRIC, "impl": "reference", "value": v, "unit": "ms", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded randn inputs, random-init weights)",
-        "config": {"workload": "wan1.3b-30L-cfg2-N32760 (bounded CPU sample, FLOP-extrapolated)", "global_batch": BATCH,
-                   "seq_len": seq_len(), "parallelism": "host cores"},
+        "config": {"workload": "cfg3: Wan2.1-1.3B 30-layer DiT forward, CFG batch 2, N=32760/sample",
+                   "model": "Wan2.1-1.3B (random init)", "layers": args.layers, "global_batch": BATCH,
+                   "seq_len": seq_len(), "latent": list(LATENT), "context": list(TEXT), "t": T_STEP,
+                   "parallelism": "host cores (bounded sample, FLOP-extrapolated)"},
         "cpu_baseline": base,
         "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "The reference's fused path needs coda-kernels (rapier, unpinned, not installable offline) and "

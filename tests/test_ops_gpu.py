@@ -74,7 +74,9 @@ def test_gemm_act_layernorm_fold(pkg, offset):
 
 
 @pytest.mark.parametrize("M,N,K,gate,inplace", [(129, 1536, 1536, True, True), (4095, 1536, 8960, True, False),
-                                                (300, 512, 256, False, True), (1, 256, 64, True, True)])
+                                                (300, 512, 256, False, True), (1, 256, 64, True, True),
+                                                (777, 64, 512, True, False), (777, 320, 512, True, True),
+                                                (513, 448, 4096, False, False)])
 def test_gemm_residual(pkg, M, N, K, gate, inplace):
     a = rand((M, K), seed=10)
     w = rand((N, K), 0.02, seed=11)
@@ -97,7 +99,8 @@ def test_gemm_residual(pkg, M, N, K, gate, inplace):
         assert got.data_ptr() == c.data_ptr()
 
 
-@pytest.mark.parametrize("M,N,K", [(257, 512, 256), (1000, 64, 4096), (4095, 8960, 1536), (32760, 8960, 1536)])
+@pytest.mark.parametrize("M,N,K", [(257, 512, 256), (1000, 64, 4096), (4095, 8960, 1536), (32760, 8960, 1536),
+                                   (513, 320, 1536)])
 def test_gemm_act_cta_pair(pkg, M, N, K):
     """CTA-pair (256-row tiles, incl. a trailing half past M) vs single-CTA tiles vs fp32."""
     a = rand((M, K), seed=30)

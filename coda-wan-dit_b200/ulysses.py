@@ -36,21 +36,30 @@ def _round256(n: int) -> int:
     return (n + 255) // 256 * 256
 
 
+def exchange_layout(B: int, Lp: int, H: int, hd: int, P: int) -> dict:
+    """Byte layout of one rank's exchange region: full[2][3][U][L][hd] bf16, y[2][B*Lp][H*hd]
+    bf16, flags[2][P] u32; every part 256-byte aligned (the kernels check it)."""
+    U, L, D = B * H // P, P * Lp, H * hd
+    full_bytes = 3 * U * L * hd * 2
+    y_bytes = B * Lp * D * 2
+    fr, yr, fl = _round256(full_bytes), _round256(y_bytes), _round256(4 * P)
+    return {
+        "full_bytes": full_bytes, "y_bytes": y_bytes,
+        "full_off": (0, fr), "y_off": (2 * fr, 2 * fr + yr), "flag_off": (2 * fr + 2 * yr, 2 * fr + 2 * yr + fl),
+        "total": 2 * fr + 2 * yr + 2 * fl,
+    }
+
+
 class _Exchange:
     """One rank's exchange region (mapped into every peer) for one (B, Lp, H, hd) shape."""
 
     def __init__(self, sp: "SeqParallel", B: int, Lp: int, H: int, hd: int, device):
         P, r = sp.world, sp.rank
         self.shape = (B, Lp, H, hd)
-        U, L, D = B * H // P, P * Lp, H * hd
-        self.full_bytes = 3 * U * L * hd * 2
-        self.y_bytes = B * Lp * D * 2
-        fr, yr = _round256(self.full_bytes), _round256(self.y_bytes)
-        self.full_off = (0, fr)
-        self.y_off = (2 * fr, 2 * fr + yr)
-        self.flag_off = (2 * fr + 2 * yr, 2 * fr + 2 * yr + _round256(4 * P))
-        total = self.flag_off[1] + _round256(4 * P)
-        self.region = torch.empty(total, dtype=torch.uint8, device=device)
+        lay = exchange_layout(B, Lp, H, hd, P)
+        self.full_bytes, self.y_bytes = lay["full_bytes"], lay["y_bytes"]
+        self.full_off, self.y_off, self.flag_off = lay["full_off"], lay["y_off"], lay["flag_off"]
+        self.region = torch.empty(lay["total"], dtype=torch.uint8, device=device)
         self.region[self.flag_off[0]:].zero_()
         self.done = torch.zeros(2, dtype=torch.int32, device=device)
         lib = _lib.load()

@@ -68,3 +68,22 @@ def test_regroup_equals_full_attention(world, B, H):
     for r in range(world):
         want = ref[:, r * Lp:(r + 1) * Lp].reshape(B * Lp, H * hd)
         assert torch.allclose(ret[r], want, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("B,Lp,H,P", [(2, 16380, 12, 2), (2, 4095, 12, 8), (2, 8190, 40, 4), (1, 7, 12, 3)])
+def test_p2p_exchange_layout(pkg, B, Lp, H, P):
+    """The NVLink exchange region: 256-byte aligned, disjoint parts that hold exactly the
+    q/k/v of this rank's units for all tokens (twice) and the attention rows of its tokens."""
+    if (B * H) % P:
+        pytest.skip("units do not divide")
+    hd = 128
+    lay = pkg.ulysses.exchange_layout(B, Lp, H, hd, P)
+    U, L = B * H // P, P * Lp
+    assert lay["full_bytes"] == 3 * U * L * hd * 2 and lay["y_bytes"] == B * Lp * H * hd * 2
+    parts = [(o, lay["full_bytes"]) for o in lay["full_off"]] + [(o, lay["y_bytes"]) for o in lay["y_off"]] + \
+        [(o, 4 * P) for o in lay["flag_off"]]
+    for o, n in parts:
+        assert o % 256 == 0 and o + n <= lay["total"]
+    spans = sorted(parts)
+    for (o1, n1), (o2, _) in zip(spans, spans[1:]):
+        assert o1 + n1 <= o2

@@ -3,7 +3,7 @@
 //   D[M, N] = A[M, K] . B[N, K]^T      A, B bf16 K-major (B = nn.Linear.weight layout),
 //                                       fp32 accumulation in TMEM.
 //
-// CTA = 10 warps, one CTA per SM, grid = the co-resident CTA count, static tile order
+// CTA = 10 warps (320 threads), one CTA per SM, grid = the co-resident CTA count, static tile order
 // tile -> (m_blk = tile / n_blocks, n_blk = tile % n_blocks):
 //   warp 0     TMA producer: A (128x64) and B (256x64) tiles, 128-byte swizzle,
 //              STAGES-deep shared-memory ring (full/empty mbarriers).

@@ -198,8 +198,8 @@ int wdit_qk_rms_rope_from_partials(void* qk, int ldqk, const float* partial, int
  * cos/sin (fp32) of the 3D RoPE for grid (f, h, w), T = f*h*w tokens, from the per-axis complex
  * frequency table freqs[max_pos, 64] (complex128 stored as interleaved fp64 (re, im) pairs);
  * the 64 pairs split [22, 21, 21] between the frame, height and width axes. Layout: token-major
- * [T, 64] (pair_major = 0, the reference's layout) or pair-major [64, T] (pair_major = 1, what
- * wdit_gemm_norm reads).
+ * [T, 64] (pair_major = 0, the reference's layout, what wdit_gemm_norm and the exchange kernels
+ * read) or pair-major [64, T] (pair_major = 1).
  * Replaces: coda_wan/wan_coda_kernels.py:414-430 build_wan_rope_table.
  */
 int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, int pair_major, float* cos_out,

@@ -114,43 +114,65 @@ __device__ __forceinline__ void load_vec8(const float* __restrict__ v, int k0, f
 }
 
 // ---------------------------------------------------------------------------
+// Grid-stride over rows: the block first stages the combined multiplier m[k] = mult_c +
+// mult_a[k] + mult_b[k] and shift s[k] = shift_a[k] + shift_b[k] in shared memory (2 K
+// floats), then every warp streams whole rows of W (all of a row's 16-byte loads issued before
+// the first use), writes bf16(W m) and reduces its column sum and s . W. The per-row vector
+// traffic comes from shared memory, so the kernel moves only W in and W' out.
 __global__ void __launch_bounds__(256)
     fold_weight_kernel(const __nv_bfloat16* __restrict__ W, int ldw, int N, int K, float mult_c,
                        const float* __restrict__ ma, const float* __restrict__ mb, const float* __restrict__ sa,
                        const float* __restrict__ sb, const float* __restrict__ bias, __nv_bfloat16* __restrict__ Wout,
                        int ldo, float* __restrict__ csum, float* __restrict__ vec) {
-  const int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (n >= N) return;
-  float cs = 0.f, vs = 0.f;
-  for (int k0 = lane * 8; k0 < K; k0 += 256) {
-    float w[8];
-    load8(W, true, static_cast<size_t>(n) * ldw + k0, w);
-    float a8[8], b8[8], s8[8], t8[8];
-    load_vec8(ma, k0, a8);
-    load_vec8(mb, k0, b8);
-    load_vec8(sa, k0, s8);
-    load_vec8(sb, k0, t8);
-    float m[8], sh[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      m[i] = mult_c + (a8[i] + b8[i]);
-      sh[i] = s8[i] + t8[i];
-    }
-    float wf[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      wf[i] = __bfloat162float(__float2bfloat16_rn(w[i] * m[i]));
-      cs += wf[i];
-      vs = fmaf(sh[i], w[i], vs);
-    }
-    store8_bf16(Wout, static_cast<size_t>(n) * ldo + k0, wf);
+  extern __shared__ float fold_smem[];
+  float* sm_m = fold_smem;      // [K]
+  float* sm_s = fold_smem + K;  // [K]
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    sm_m[k] = mult_c + ((ma != nullptr ? ma[k] : 0.f) + (mb != nullptr ? mb[k] : 0.f));
+    sm_s[k] = (sa != nullptr ? sa[k] : 0.f) + (sb != nullptr ? sb[k] : 0.f);
   }
-  cs = warp_sum(cs);
-  vs = warp_sum(vs);
-  if (lane == 0) {
-    csum[n] = cs;
-    vec[n] = vs + (bias != nullptr ? bias[n] : 0.f);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  constexpr int kVec = 6;  // 16-byte vectors per lane in flight (K = 1536 in one pass)
+  for (int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5); n < N; n += gridDim.x * kRowsPerBlock) {
+    float cs = 0.f, vs = 0.f;
+    const __nv_bfloat16* wr = W + static_cast<size_t>(n) * ldw;
+    for (int c0 = lane * 8; c0 < K; c0 += kVec * 256) {
+      uint4 raw[kVec];
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) {
+        if (c0 + u * 256 < K) raw[u] = *reinterpret_cast<const uint4*>(wr + c0 + u * 256);
+      }
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) {
+        const int k0 = c0 + u * 256;
+        if (k0 >= K) break;
+        const float4 m0 = *reinterpret_cast<const float4*>(sm_m + k0);
+        const float4 m1 = *reinterpret_cast<const float4*>(sm_m + k0 + 4);
+        const float4 s0 = *reinterpret_cast<const float4*>(sm_s + k0);
+        const float4 s1 = *reinterpret_cast<const float4*>(sm_s + k0 + 4);
+        const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+        const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[u]);
+        float wf[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          wf[2 * i] = __bfloat162float(__float2bfloat16_rn(f.x * m[2 * i]));
+          wf[2 * i + 1] = __bfloat162float(__float2bfloat16_rn(f.y * m[2 * i + 1]));
+          cs += wf[2 * i] + wf[2 * i + 1];
+          vs = fmaf(sh[2 * i], f.x, vs);
+          vs = fmaf(sh[2 * i + 1], f.y, vs);
+        }
+        store8_bf16(Wout, static_cast<size_t>(n) * ldo + k0, wf);
+      }
+    }
+    cs = warp_sum(cs);
+    vs = warp_sum(vs);
+    if (lane == 0) {
+      csum[n] = cs;
+      vec[n] = vs + (bias != nullptr ? bias[n] : 0.f);
+    }
   }
 }
 
@@ -396,7 +418,22 @@ int wdit_fold_weight(const void* W, int ldw, int N, int K, float mult_c, const f
   if (!a16(W) || !a16(W_out) || ldw % 8 != 0 || ldw_out % 8 != 0) return WDIT_ERR_ALIGN;
   if ((mult_a && !a16(mult_a)) || (mult_b && !a16(mult_b)) || (shift_a && !a16(shift_a)) || (shift_b && !a16(shift_b)))
     return WDIT_ERR_ALIGN;
-  fold_weight_kernel<<<row_blocks(N), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  const size_t smem = static_cast<size_t>(K) * 2 * sizeof(float);
+  if (smem > 48 * 1024) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev & 63]) {
+      cudaFuncSetAttribute(fold_weight_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      attr_set[dev & 63] = true;
+    }
+  }
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  unsigned blocks = row_blocks(N);
+  if (blocks > static_cast<unsigned>(4 * sms)) blocks = static_cast<unsigned>(4 * sms);
+  fold_weight_kernel<<<blocks, 256, smem, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(W), ldw, N, K, mult_c, mult_a, mult_b, shift_a, shift_b, bias,
       reinterpret_cast<__nv_bfloat16*>(W_out), ldw_out, csum_out, vec_out);
   return launch_status();

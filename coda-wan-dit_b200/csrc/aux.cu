@@ -100,19 +100,6 @@ __global__ void __launch_bounds__(256) ln_stats_kernel(const void* __restrict__ 
   }
 }
 
-// 8 consecutive fp32 of an optional vector (zeros when absent), two 16-byte loads.
-__device__ __forceinline__ void load_vec8(const float* __restrict__ v, int k0, float (&out)[8]) {
-  if (v == nullptr) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) out[i] = 0.f;
-    return;
-  }
-  const float4 x = __ldg(reinterpret_cast<const float4*>(v + k0));
-  const float4 y = __ldg(reinterpret_cast<const float4*>(v + k0) + 1);
-  out[0] = x.x; out[1] = x.y; out[2] = x.z; out[3] = x.w;
-  out[4] = y.x; out[5] = y.y; out[6] = y.z; out[7] = y.w;
-}
-
 // ---------------------------------------------------------------------------
 // Grid-stride over rows: the block first stages the combined multiplier m[k] = mult_c +
 // mult_a[k] + mult_b[k] and shift s[k] = shift_a[k] + shift_b[k] in shared memory (2 K

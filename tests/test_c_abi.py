@@ -65,3 +65,24 @@ def test_norm_workspace_size(lib):
     part = ((M * groups * (width // 128) * 4 + 255) // 256) * 256
     assert lib.wdit_gemm_norm_workspace_bytes(M, 4608, groups, width) == part
     assert lib.wdit_stats_tile_width() == 256
+
+
+def test_p2p_argument_validation_without_device(lib):
+    null = ctypes.c_void_p(None)
+    dummy = ctypes.c_void_p(0x1000)
+    peers = (ctypes.c_void_p * 2)(0x100000, 0x200000)
+    # NULL operands -> WDIT_ERR_ARG
+    assert lib.wdit_p2p_qkv_exchange(null, 4608, dummy, 24, dummy, dummy, 1e-6, dummy, dummy, 64, 2, 96, 12, 128, 2, 0,
+                                     peers, 0, 0, 1, dummy, null) == 1
+    # head_dim other than 128, units that do not divide over the ranks -> WDIT_ERR_SHAPE
+    assert lib.wdit_p2p_qkv_exchange(dummy, 4608, dummy, 24, dummy, dummy, 1e-6, dummy, dummy, 64, 2, 96, 12, 64, 2, 0,
+                                     peers, 0, 0, 1, dummy, null) == 2
+    assert lib.wdit_p2p_qkv_exchange(dummy, 4608, dummy, 24, dummy, dummy, 1e-6, dummy, dummy, 64, 1, 96, 12, 128, 8, 0,
+                                     peers, 0, 0, 1, dummy, null) == 2
+    # a rank outside [0, P) -> WDIT_ERR_SHAPE; misaligned region offsets -> WDIT_ERR_ALIGN
+    assert lib.wdit_p2p_out_exchange(dummy, 128, 128, 2, 96, 12, 128, 2, 2, peers, 0, 1536, 0, 1, dummy, null) == 2
+    assert lib.wdit_p2p_out_exchange(dummy, 128, 128, 2, 96, 12, 128, 2, 0, peers, 100, 1536, 0, 1, dummy, null) == 3
+    assert lib.wdit_p2p_wait(null, 2, 1, null) == 1
+    assert lib.wdit_p2p_wait(dummy, 0, 1, null) == 2
+    assert lib.wdit_ipc_handle(null, null, None) == 1
+    assert lib.wdit_ipc_open(null, None) == 1

@@ -65,15 +65,30 @@ _SIGNATURES = {
     "wdit_static_scratch_bytes": (c_longlong, []),
     "wdit_ln_stats": (c_int, [P, I, I, I, I, P, P, P, P]),
     "wdit_fold_weight": (c_int, [P, I, I, I, F, P, P, P, P, P, P, I, P, P, P]),
+    "wdit_fold_weight_batch": (c_int, [P, I, P]),
     "wdit_layernorm_modulation": (c_int, [P, I, I, I, I, P, P, F, P, I, P]),
     "wdit_rmsnorm": (c_int, [P, I, I, I, P, F, P, I, P]),
     "wdit_qk_rms_rope_from_partials": (c_int, [P, I, P, I, I, P, P, P, P, F, P]),
+    "wdit_rms_apply_layers": (c_int, [P, I, I, P, I, I, P, F, I, c_longlong, I, I, P]),
     "wdit_rope_table": (c_int, [P, I, I, I, I, I, P, P, P]),
     "wdit_ulysses_pack": (c_int, [P, I, I, I, I, I, I, I, P, P]),
     "wdit_seq_gather": (c_int, [P, I, I, I, I, I, P, P]),
     "wdit_seq_scatter": (c_int, [P, c_longlong, c_longlong, I, I, I, I, P, P]),
     "wdit_ulysses_unpack": (c_int, [P, I, I, I, I, I, P, I, P]),
 }
+
+
+class FoldJob(ctypes.Structure):
+    """struct wdit_fold_job of include/wdit.h."""
+
+    _fields_ = [
+        ("W", c_void_p), ("ldw", c_int), ("N", c_int), ("K", c_int), ("mult_c", c_float),
+        ("mult_a", c_void_p), ("mult_b", c_void_p), ("shift_a", c_void_p), ("shift_b", c_void_p),
+        ("bias", c_void_p), ("W_out", c_void_p), ("ldw_out", c_int), ("csum_out", c_void_p), ("vec_out", c_void_p),
+    ]
+
+
+FOLD_JOBS_PER_LAUNCH = 64
 
 
 def library_path() -> Path:
@@ -124,6 +139,7 @@ def check(rc: int, what: str) -> None:
 # Entry points that launch device work (counted by launch_counter for the benchmark).
 _LAUNCHING = {
     "wdit_gemm_act", "wdit_gemm_residual", "wdit_gemm_norm", "wdit_ln_stats", "wdit_fold_weight",
+    "wdit_fold_weight_batch", "wdit_rms_apply_layers",
     "wdit_layernorm_modulation", "wdit_rmsnorm", "wdit_qk_rms_rope_from_partials", "wdit_rope_table",
     "wdit_ulysses_pack", "wdit_seq_gather", "wdit_seq_scatter", "wdit_ulysses_unpack",
     "wdit_p2p_qkv_exchange", "wdit_p2p_out_exchange", "wdit_p2p_wait",

@@ -9,13 +9,14 @@ Counterpart of coda_wan/run_wan_coda.py:82-205 (CodaFullBlock).
 
 Per block, on one stream (M = B * L rows):
 
-    fold QKV weight      W' = W * (1 + mod1 + e1), csum, vec = (mod0 + e0)^T W + b
+    fold QKV weight      W' = W * (1 + mod1 + e1), csum, vec = (mod0 + e0)^T W + b (inside a
+                         model the folds of all blocks run in one launch per step instead)
     QKV GEMM             LN absorbed + bias -> qkv bf16 + q/k mean-square partials, then the
                          in-place full-width q/k RMSNorm + 3D RoPE pass
     self-attention       PyTorch SDPA (or the Ulysses all-to-all around it)
     self-O GEMM          x += (y Wo^T + bo) * (mod2 + e2)   -> x fp32, bf16 copy, LN stats
     cross-Q GEMM         norm3 folded statically (gamma into W, beta into vec) + RMSNorm
-    cross-KV GEMM        context -> k (RMSNorm), v
+    cross-KV GEMM        context -> k (RMSNorm), v (inside a model: one GEMM for all blocks)
     cross-attention      PyTorch SDPA
     cross-O GEMM         x += cy Wco^T + bco                 -> x, bf16 copy, LN stats
     fold FFN1 weight     as QKV with (mod4 + e4, mod3 + e3)
@@ -122,6 +123,12 @@ class FusedWanBlock(nn.Module):
         self.workspace = None  # None: the per-device shared workspace (launches are stream-ordered)
         self.seq_parallel = None  # set by the model for token-sharded runs
         self.kernel_timer = None  # list: (start event, end event, flops) of each FFN1 GEMM launch
+        # (e, folds) set by the model for the next forward: this step's QKV / FFN1 weight folds,
+        # computed for all blocks in one launch (`fold_specs`); used when forward gets that e.
+        self._prefolded = None
+        # (context, kv) set by the model: this block's cross-attention K (normalized) and V,
+        # projected for all blocks in one GEMM; used when forward gets that context.
+        self._pre_ckv = None
 
         # Zero-copy where the weights are already bf16: QKV and cross-KV are packed into
         # one allocation each and the Linear parameters become views of it.
@@ -214,6 +221,39 @@ class FusedWanBlock(nn.Module):
             ops.ln_stats(xb, stats_out=stats, x_f32_out=x32)
         return x32, xb, stats
 
+    def fold_specs(self, e: torch.Tensor) -> list[dict]:
+        """The per-step adaLN weight folds of this block for modulation e [Be, 6, D]
+        (`ops.fold_weight_batch` specs): QKV then FFN1 for each of the Be entries."""
+        D = self.dim
+        ev = e.float().reshape(-1, 6 * D).contiguous()
+        mod = self.mod
+        specs = []
+        for b in range(ev.shape[0]):
+            specs.append(dict(w=self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=ev[b, D:2 * D], shift_a=mod[0],
+                              shift_b=ev[b, :D], bias=self.b_qkv))
+            specs.append(dict(w=self.w_1, mult_c=1.0, mult_a=mod[4], mult_b=ev[b, 4 * D:5 * D], shift_a=mod[3],
+                              shift_b=ev[b, 3 * D:4 * D], bias=self.b_1))
+        return specs
+
+    def adopt_cross_kv(self, w: torch.Tensor, b: torch.Tensor, wk: torch.Tensor) -> None:
+        """Move the packed cross-attention K/V weight, its fp32 bias and the K norm weight into
+        the given storage (the model's all-blocks allocations; same values). The wrapped module's
+        bf16 K/V weights, views of the old packed weight, become views of the new one."""
+        ca, d = self.inner.cross_attn, self.dim
+        if ca.k.weight.dtype == torch.bfloat16 and ca.k.weight.untyped_storage().data_ptr() == \
+                self.w_ckv.untyped_storage().data_ptr():
+            ops.replace_parameter_with_view(ca.k, "weight", w[:d])
+            ops.replace_parameter_with_view(ca.v, "weight", w[d:])
+        self.w_ckv, self.b_ckv, self.w_cnk = w, b, wk
+
+    def set_cross_kv(self, context: torch.Tensor, kv: torch.Tensor) -> None:
+        """Hand this block its cross-attention K/V of `context` for its next forward."""
+        self._pre_ckv = (context, kv)
+
+    def set_prefolded(self, e: torch.Tensor, folds: list) -> None:
+        """Hand this block the results of its `fold_specs(e)` for its next forward."""
+        self._prefolded = (e, folds)
+
     def forward(self, x, e, seq_lens, grid_sizes, freqs, context, context_lens):
         B, L, D = x.shape
         H, hd = self.num_heads, self.head_dim
@@ -228,6 +268,8 @@ class FusedWanBlock(nn.Module):
         assert Be in (1, B), "e must have batch 1 (shared modulation) or the block's batch"
         ev = ev.contiguous()
         mod = self.mod
+        pre, self._prefolded = self._prefolded, None
+        folds = pre[1] if pre is not None and pre[0] is e and len(pre[1]) == 2 * Be else None
         gate_stride = 6 * D
         rows_per_batch = L if Be == B and B > 1 else M
 
@@ -251,8 +293,11 @@ class FusedWanBlock(nn.Module):
         part = torch.empty((M, 2 * D // ops.RMS_BLOCK), dtype=torch.float32, device=dev) if fused_exchange else None
         for b in range(Be):
             r0, r1 = (0, M) if Be == 1 else (b * L, (b + 1) * L)
-            wf, cs, vec = ops.fold_weight(self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=e_row(b, 1),
-                                          shift_a=mod[0], shift_b=e_row(b, 0), bias=self.b_qkv)
+            if folds is not None:
+                wf, cs, vec = folds[2 * b]
+            else:
+                wf, cs, vec = ops.fold_weight(self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=e_row(b, 1),
+                                              shift_a=mod[0], shift_b=e_row(b, 0), bias=self.b_qkv)
             ln = ops.LnFold(cs, stats[r0:r1], self.eps)
             if fused_exchange:
                 ops.gemm_act(xb[r0:r1], wf, vec=vec, ln=ln, out=qkv[r0:r1], ms_out=part[r0:r1], ms_cols=2 * D)
@@ -286,11 +331,15 @@ class FusedWanBlock(nn.Module):
             cq = ops.gemm_norm(xb, self.w_cq, vec=self.vec_cq, norm_groups=1, norm_width=D,
                                norm_w=(self.w_cnq, None), norm_eps=self.rms_eps, workspace=self.workspace)
         Bc, Lc, _ = context.shape
-        ctx = context.reshape(Bc * Lc, D)
-        if ctx.dtype != torch.bfloat16:
-            ctx = ctx.to(torch.bfloat16)
-        ckv = ops.gemm_norm(ctx, self.w_ckv, vec=self.b_ckv, norm_groups=1, norm_width=D,
-                            norm_w=(self.w_cnk, None), norm_eps=self.rms_eps, workspace=self.workspace)
+        pre_kv, self._pre_ckv = self._pre_ckv, None
+        if pre_kv is not None and pre_kv[0] is context:
+            ckv = pre_kv[1]
+        else:
+            ctx = context.reshape(Bc * Lc, D)
+            if ctx.dtype != torch.bfloat16:
+                ctx = ctx.to(torch.bfloat16)
+            ckv = ops.gemm_norm(ctx, self.w_ckv, vec=self.b_ckv, norm_groups=1, norm_width=D,
+                                norm_w=(self.w_cnk, None), norm_eps=self.rms_eps, workspace=self.workspace)
         ck = ckv[:, :D].view(Bc, Lc, H, hd)
         cv = ckv[:, D:].view(Bc, Lc, H, hd)
         cy = local_attention(cq.view(B, L, H, hd), ck, cv, context_lens).reshape(M, D)
@@ -300,8 +349,11 @@ class FusedWanBlock(nn.Module):
         h = torch.empty((M, self.ffn_dim), dtype=torch.bfloat16, device=dev)
         for b in range(Be):
             r0, r1 = (0, M) if Be == 1 else (b * L, (b + 1) * L)
-            wf, cs, vec = ops.fold_weight(self.w_1, mult_c=1.0, mult_a=mod[4], mult_b=e_row(b, 4),
-                                          shift_a=mod[3], shift_b=e_row(b, 3), bias=self.b_1)
+            if folds is not None:
+                wf, cs, vec = folds[2 * b + 1]
+            else:
+                wf, cs, vec = ops.fold_weight(self.w_1, mult_c=1.0, mult_a=mod[4], mult_b=e_row(b, 4),
+                                              shift_a=mod[3], shift_b=e_row(b, 3), bias=self.b_1)
             timer = self.kernel_timer
             if timer is not None:
                 ev0 = torch.cuda.Event(enable_timing=True)

@@ -4,7 +4,8 @@
 //   ln_stats_kernel      per-256-column (mean, M2) of the first block's input rows
 //                        (+ bf16 / fp32 copies); stats format = wdit_gemm_residual's.
 //   fold_weight_kernel   per-step adaLN fold into the next Linear: W' = W * mult[k],
-//                        csum[n] = sum_k W'[n,k], vec[n] = sum_k shift[k] W[n,k] + b[n].
+//                        csum[n] = sum_k W'[n,k], vec[n] = sum_k shift[k] W[n,k] + b[n];
+//   fold_batch_kernel    the same for up to 64 weights in one launch (a whole forward step).
 //   layernorm_mod_kernel reference op coda_wan/wan_coda_kernels.py:35-81.
 //   rmsnorm_kernel       reference op coda_wan/wan_coda_kernels.py:371-411.
 //   rms_rope_apply_kernel full-width RMSNorm (+ RoPE) from mean-square partials, in place:
@@ -101,66 +102,126 @@ __global__ void __launch_bounds__(256) ln_stats_kernel(const void* __restrict__ 
 }
 
 // ---------------------------------------------------------------------------
-// Grid-stride over rows: the block first stages the combined multiplier m[k] = mult_c +
-// mult_a[k] + mult_b[k] and shift s[k] = shift_a[k] + shift_b[k] in shared memory (2 K
-// floats), then every warp streams whole rows of W (all of a row's 16-byte loads issued before
-// the first use), writes bf16(W m) and reduces its column sum and s . W. The per-row vector
-// traffic comes from shared memory, so the kernel moves only W in and W' out.
-__global__ void __launch_bounds__(256)
-    fold_weight_kernel(const __nv_bfloat16* __restrict__ W, int ldw, int N, int K, float mult_c,
-                       const float* __restrict__ ma, const float* __restrict__ mb, const float* __restrict__ sa,
-                       const float* __restrict__ sb, const float* __restrict__ bias, __nv_bfloat16* __restrict__ Wout,
-                       int ldo, float* __restrict__ csum, float* __restrict__ vec) {
-  extern __shared__ float fold_smem[];
-  float* sm_m = fold_smem;      // [K]
-  float* sm_s = fold_smem + K;  // [K]
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    sm_m[k] = mult_c + ((ma != nullptr ? ma[k] : 0.f) + (mb != nullptr ? mb[k] : 0.f));
-    sm_s[k] = (sa != nullptr ? sa[k] : 0.f) + (sb != nullptr ? sb[k] : 0.f);
+// Weight fold. One fold job: W[N,K] -> W'[N,K], csum[N], vec[N] (the arguments of wdit_fold_weight).
+struct FoldJob {
+  const __nv_bfloat16* W;
+  const float* ma;
+  const float* mb;
+  const float* sa;
+  const float* sb;
+  const float* bias;
+  __nv_bfloat16* Wout;
+  float* csum;
+  float* vec;
+  int ldw, N, K, ldo;
+  float mult_c;
+};
+
+// The job's multiplier / shift vectors into shared memory (2 K floats).
+__device__ __forceinline__ void fold_load_vectors(const FoldJob& j, float* sm_m, float* sm_s) {
+  for (int k = threadIdx.x; k < j.K; k += blockDim.x) {
+    sm_m[k] = j.mult_c + ((j.ma != nullptr ? j.ma[k] : 0.f) + (j.mb != nullptr ? j.mb[k] : 0.f));
+    sm_s[k] = (j.sa != nullptr ? j.sa[k] : 0.f) + (j.sb != nullptr ? j.sb[k] : 0.f);
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  constexpr int kVec = 6;  // 16-byte vectors per lane in flight (K = 1536 in one pass)
-  for (int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5); n < N; n += gridDim.x * kRowsPerBlock) {
-    float cs = 0.f, vs = 0.f;
-    const __nv_bfloat16* wr = W + static_cast<size_t>(n) * ldw;
-    for (int c0 = lane * 8; c0 < K; c0 += kVec * 256) {
-      uint4 raw[kVec];
+}
+
+// One row chunk of kFoldVec 16-byte vectors per lane (K <= kFoldVec * 256 in one chunk):
+// bf16(W m) stored, the column sum and s . W accumulated.
+constexpr int kFoldVec = 6;
+__device__ __forceinline__ void fold_chunk(const FoldJob& j, const float* sm_m, const float* sm_s, int n, int c0,
+                                           const uint4 (&raw)[kFoldVec], float& cs, float& vs) {
 #pragma unroll
-      for (int u = 0; u < kVec; ++u) {
-        if (c0 + u * 256 < K) raw[u] = *reinterpret_cast<const uint4*>(wr + c0 + u * 256);
-      }
+  for (int u = 0; u < kFoldVec; ++u) {
+    const int k0 = c0 + u * 256;
+    if (k0 >= j.K) break;
+    const float4 m0 = *reinterpret_cast<const float4*>(sm_m + k0);
+    const float4 m1 = *reinterpret_cast<const float4*>(sm_m + k0 + 4);
+    const float4 s0 = *reinterpret_cast<const float4*>(sm_s + k0);
+    const float4 s1 = *reinterpret_cast<const float4*>(sm_s + k0 + 4);
+    const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+    const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[u]);
+    float wf[8];
 #pragma unroll
-      for (int u = 0; u < kVec; ++u) {
-        const int k0 = c0 + u * 256;
-        if (k0 >= K) break;
-        const float4 m0 = *reinterpret_cast<const float4*>(sm_m + k0);
-        const float4 m1 = *reinterpret_cast<const float4*>(sm_m + k0 + 4);
-        const float4 s0 = *reinterpret_cast<const float4*>(sm_s + k0);
-        const float4 s1 = *reinterpret_cast<const float4*>(sm_s + k0 + 4);
-        const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-        const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[u]);
-        float wf[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(h[i]);
-          wf[2 * i] = __bfloat162float(__float2bfloat16_rn(f.x * m[2 * i]));
-          wf[2 * i + 1] = __bfloat162float(__float2bfloat16_rn(f.y * m[2 * i + 1]));
-          cs += wf[2 * i] + wf[2 * i + 1];
-          vs = fmaf(sh[2 * i], f.x, vs);
-          vs = fmaf(sh[2 * i + 1], f.y, vs);
-        }
-        store8_bf16(Wout, static_cast<size_t>(n) * ldo + k0, wf);
-      }
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      wf[2 * i] = __bfloat162float(__float2bfloat16_rn(f.x * m[2 * i]));
+      wf[2 * i + 1] = __bfloat162float(__float2bfloat16_rn(f.y * m[2 * i + 1]));
+      cs += wf[2 * i] + wf[2 * i + 1];
+      vs = fmaf(sh[2 * i], f.x, vs);
+      vs = fmaf(sh[2 * i + 1], f.y, vs);
     }
-    cs = warp_sum(cs);
-    vs = warp_sum(vs);
-    if (lane == 0) {
-      csum[n] = cs;
-      vec[n] = vs + (bias != nullptr ? bias[n] : 0.f);
-    }
+    store8_bf16(j.Wout, static_cast<size_t>(n) * j.ldo + k0, wf);
   }
+}
+
+__device__ __forceinline__ void fold_load_chunk(const FoldJob& j, int n, int c0, uint4 (&raw)[kFoldVec]) {
+  const __nv_bfloat16* wr = j.W + static_cast<size_t>(n) * j.ldw;
+#pragma unroll
+  for (int u = 0; u < kFoldVec; ++u) {
+    if (c0 + u * 256 < j.K) raw[u] = *reinterpret_cast<const uint4*>(wr + c0 + u * 256);
+  }
+}
+
+__device__ __forceinline__ void fold_finish_row(const FoldJob& j, int n, float cs, float vs) {
+  cs = warp_sum(cs);
+  vs = warp_sum(vs);
+  if ((threadIdx.x & 31) == 0) {
+    j.csum[n] = cs;
+    j.vec[n] = vs + (j.bias != nullptr ? j.bias[n] : 0.f);
+  }
+}
+
+// Rows n = n0 + warp, n0 + warp + n_step, ... below n1, one warp per row streamed in chunks of
+// kFoldVec 16-byte vectors per lane (one chunk for K <= 1536), all of a chunk's loads issued
+// before the first use.
+__device__ __forceinline__ void fold_rows(const FoldJob& j, const float* sm_m, const float* sm_s, int n0, int n1,
+                                          int n_step) {
+  const int c_lane = (threadIdx.x & 31) * 8;
+  for (int n = n0 + (threadIdx.x >> 5); n < n1; n += n_step) {
+    float cs = 0.f, vs = 0.f;
+    for (int c0 = c_lane; c0 < j.K; c0 += kFoldVec * 256) {
+      uint4 raw[kFoldVec];
+      fold_load_chunk(j, n, c0, raw);
+      fold_chunk(j, sm_m, sm_s, n, c0, raw, cs, vs);
+    }
+    fold_finish_row(j, n, cs, vs);
+  }
+}
+
+// Single fold: the multiplier m[k] = mult_c + mult_a[k] + mult_b[k] and shift s[k] = shift_a[k]
+// + shift_b[k] are built once per block in shared memory, then the block's warps stream
+// whole rows of W (grid-stride), write bf16(W m) and reduce each row's column sum and s . W.
+// The per-row vector traffic comes from shared memory, so the kernel moves only W in and W' out.
+__global__ void __launch_bounds__(256) fold_weight_kernel(const __grid_constant__ FoldJob job) {
+  extern __shared__ float fold_smem[];
+  fold_load_vectors(job, fold_smem, fold_smem + job.K);
+  fold_rows(job, fold_smem, fold_smem + job.K, blockIdx.x * kRowsPerBlock, job.N, gridDim.x * kRowsPerBlock);
+}
+
+// All of a forward step's folds in one launch. Job i owns blocks [first[i], first[i+1]); each
+// block folds kFoldRowsPerCta consecutive rows of its job. Up to kMaxFoldJobs jobs per launch
+// (the descriptors travel as the kernel parameter, ~6 KB).
+constexpr int kMaxFoldJobs = 64;
+constexpr int kFoldRowsPerCta = 64;
+struct FoldBatch {
+  FoldJob job[kMaxFoldJobs];
+  int first[kMaxFoldJobs + 1];
+  int n;
+};
+
+__global__ void __launch_bounds__(256) fold_batch_kernel(const __grid_constant__ FoldBatch b) {
+  extern __shared__ float fold_smem[];
+  int lo = 0, hi = b.n - 1;  // the job whose block range holds blockIdx.x
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (b.first[mid] <= static_cast<int>(blockIdx.x)) lo = mid; else hi = mid - 1;
+  }
+  const FoldJob& job = b.job[lo];
+  fold_load_vectors(job, fold_smem, fold_smem + job.K);
+  const int n0 = (static_cast<int>(blockIdx.x) - b.first[lo]) * kFoldRowsPerCta;
+  fold_rows(job, fold_smem, fold_smem + job.K, n0, min(n0 + kFoldRowsPerCta, job.N), kRowsPerBlock);
 }
 
 // ---------------------------------------------------------------------------
@@ -255,10 +316,16 @@ __global__ void __launch_bounds__(32 * kApplyRowsPerBlock)
     rms_rope_apply_kernel(__nv_bfloat16* __restrict__ x, int ldx, int M, const float* __restrict__ part,
                           int part_ld, int groups, int width, const float* __restrict__ w0,
                           const float* __restrict__ w1, float eps, int rope_groups, const float* __restrict__ cs,
-                          const float* __restrict__ sn, int rope_ld, int rows_per_batch, int token_offset) {
+                          const float* __restrict__ sn, int rope_ld, int rows_per_batch, int token_offset,
+                          long long x_layer_stride, int part_layer_stride, int w_layer_stride) {
   const int row = blockIdx.x * kApplyRowsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
+  // Layer blockIdx.y: its own columns of x, partial columns and weights (one layer unless batched).
+  x += static_cast<long long>(blockIdx.y) * x_layer_stride;
+  part += static_cast<size_t>(blockIdx.y) * part_layer_stride;
+  w0 += static_cast<size_t>(blockIdx.y) * w_layer_stride;
+  if (w1 != nullptr) w1 += static_cast<size_t>(blockIdx.y) * w_layer_stride;
   const int total = groups * width;
   __nv_bfloat16* base = x + static_cast<size_t>(row) * ldx;
   uint4 raw[kApplyVec];
@@ -375,13 +442,74 @@ int launch_rms_rope_apply(void* x, int ldx, int M, const float* part, int part_l
   const unsigned blocks = static_cast<unsigned>((M + kApplyRowsPerBlock - 1) / kApplyRowsPerBlock);
   rms_rope_apply_kernel<<<blocks, 32 * kApplyRowsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<__nv_bfloat16*>(x), ldx, M, part, part_ld, groups, width, w0, w1, eps, rope_groups, rope_cos,
-      rope_sin, rope_ld, rows_per_batch, token_offset);
+      rope_sin, rope_ld, rows_per_batch, token_offset, 0ll, 0, 0);
+  return launch_status();
+}
+
+int launch_rms_apply_layers(void* x, int ldx, int M, const float* part, int part_ld, int width, const float* w,
+                            float eps, int layers, long long x_layer_stride, int part_layer_stride, int w_layer_stride,
+                            void* stream) {
+  if (x == nullptr || part == nullptr || w == nullptr) return WDIT_ERR_ARG;
+  if (M <= 0 || width <= 0 || width % 128 != 0 || layers < 1 || layers > 65535) return WDIT_ERR_SHAPE;
+  if (x_layer_stride < 0 || part_layer_stride < 0 || w_layer_stride < 0) return WDIT_ERR_SHAPE;
+  // The last layer's columns, partials and weights stay inside the row / weight table.
+  if (static_cast<long long>(layers - 1) * x_layer_stride + width > ldx) return WDIT_ERR_SHAPE;
+  if (static_cast<long long>(layers - 1) * part_layer_stride + width / 128 > part_ld) return WDIT_ERR_SHAPE;
+  if (!a16(x) || ldx % 8 != 0 || x_layer_stride % 8 != 0 || !a16(w) || w_layer_stride % 4 != 0) return WDIT_ERR_ALIGN;
+  const dim3 grid(static_cast<unsigned>((M + kApplyRowsPerBlock - 1) / kApplyRowsPerBlock), static_cast<unsigned>(layers));
+  rms_rope_apply_kernel<<<grid, 32 * kApplyRowsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<__nv_bfloat16*>(x), ldx, M, part, part_ld, 1, width, w, nullptr, eps, 0, nullptr, nullptr, 0, 1,
+      0, x_layer_stride, part_layer_stride, w_layer_stride);
   return launch_status();
 }
 
 }  // namespace wdit
 
 using namespace wdit;
+
+namespace {
+int fold_job_check(const wdit_fold_job& j) {
+  if (j.W == nullptr || j.W_out == nullptr || j.csum_out == nullptr || j.vec_out == nullptr) return WDIT_ERR_ARG;
+  if (j.N <= 0 || j.K <= 0 || j.K % 8 != 0 || j.ldw < j.K || j.ldw_out < j.K) return WDIT_ERR_SHAPE;
+  if (!a16(j.W) || !a16(j.W_out) || j.ldw % 8 != 0 || j.ldw_out % 8 != 0) return WDIT_ERR_ALIGN;
+  if ((j.mult_a && !a16(j.mult_a)) || (j.mult_b && !a16(j.mult_b)) || (j.shift_a && !a16(j.shift_a)) ||
+      (j.shift_b && !a16(j.shift_b)))
+    return WDIT_ERR_ALIGN;
+  return WDIT_OK;
+}
+
+FoldJob fold_job_dev(const wdit_fold_job& j) {
+  FoldJob d;
+  d.W = reinterpret_cast<const __nv_bfloat16*>(j.W);
+  d.ma = j.mult_a;
+  d.mb = j.mult_b;
+  d.sa = j.shift_a;
+  d.sb = j.shift_b;
+  d.bias = j.bias;
+  d.Wout = reinterpret_cast<__nv_bfloat16*>(j.W_out);
+  d.csum = j.csum_out;
+  d.vec = j.vec_out;
+  d.ldw = j.ldw;
+  d.N = j.N;
+  d.K = j.K;
+  d.ldo = j.ldw_out;
+  d.mult_c = j.mult_c;
+  return d;
+}
+
+// Dynamic shared memory above the 48 KB default (K > 6144) needs the opt-in, once per device.
+template <typename Kernel>
+void allow_fold_smem(Kernel kernel, size_t smem, bool (&done)[64]) {
+  if (smem <= 48 * 1024) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!done[dev & 63]) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    done[dev & 63] = true;
+  }
+}
+}  // namespace
+
 
 extern "C" {
 
@@ -400,30 +528,48 @@ int wdit_ln_stats(const void* x, int x_is_bf16, int ldx, int M, int D, float* st
 int wdit_fold_weight(const void* W, int ldw, int N, int K, float mult_c, const float* mult_a, const float* mult_b,
                      const float* shift_a, const float* shift_b, const float* bias, void* W_out, int ldw_out,
                      float* csum_out, float* vec_out, void* stream) {
-  if (W == nullptr || W_out == nullptr || csum_out == nullptr || vec_out == nullptr) return WDIT_ERR_ARG;
-  if (N <= 0 || K <= 0 || K % 8 != 0 || ldw < K || ldw_out < K) return WDIT_ERR_SHAPE;
-  if (!a16(W) || !a16(W_out) || ldw % 8 != 0 || ldw_out % 8 != 0) return WDIT_ERR_ALIGN;
-  if ((mult_a && !a16(mult_a)) || (mult_b && !a16(mult_b)) || (shift_a && !a16(shift_a)) || (shift_b && !a16(shift_b)))
-    return WDIT_ERR_ALIGN;
+  const wdit_fold_job j = {W, ldw, N, K, mult_c, mult_a, mult_b, shift_a, shift_b, bias, W_out, ldw_out, csum_out,
+                           vec_out};
+  const int rc = fold_job_check(j);
+  if (rc) return rc;
   const size_t smem = static_cast<size_t>(K) * 2 * sizeof(float);
-  if (smem > 48 * 1024) {
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr_set[dev & 63]) {
-      cudaFuncSetAttribute(fold_weight_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      attr_set[dev & 63] = true;
-    }
-  }
+  static bool attr_set[64] = {};
+  allow_fold_smem(fold_weight_kernel, smem, attr_set);
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   unsigned blocks = row_blocks(N);
   if (blocks > static_cast<unsigned>(4 * sms)) blocks = static_cast<unsigned>(4 * sms);
-  fold_weight_kernel<<<blocks, 256, smem, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(W), ldw, N, K, mult_c, mult_a, mult_b, shift_a, shift_b, bias,
-      reinterpret_cast<__nv_bfloat16*>(W_out), ldw_out, csum_out, vec_out);
+  fold_weight_kernel<<<blocks, 256, smem, static_cast<cudaStream_t>(stream)>>>(fold_job_dev(j));
   return launch_status();
+}
+
+int wdit_fold_weight_batch(const wdit_fold_job* jobs, int n_jobs, void* stream) {
+  if (n_jobs < 0 || (n_jobs > 0 && jobs == nullptr)) return WDIT_ERR_ARG;
+  int max_k = 0;
+  for (int i = 0; i < n_jobs; ++i) {
+    const int rc = fold_job_check(jobs[i]);
+    if (rc) return rc;
+    if (jobs[i].K > max_k) max_k = jobs[i].K;
+  }
+  const size_t smem = static_cast<size_t>(max_k) * 2 * sizeof(float);
+  static bool attr_set[64] = {};
+  allow_fold_smem(fold_batch_kernel, smem, attr_set);
+  for (int j0 = 0; j0 < n_jobs; j0 += kMaxFoldJobs) {
+    FoldBatch b;
+    b.n = n_jobs - j0 < kMaxFoldJobs ? n_jobs - j0 : kMaxFoldJobs;
+    int ctas = 0;
+    for (int i = 0; i < b.n; ++i) {
+      b.job[i] = fold_job_dev(jobs[j0 + i]);
+      b.first[i] = ctas;
+      ctas += (jobs[j0 + i].N + kFoldRowsPerCta - 1) / kFoldRowsPerCta;
+    }
+    b.first[b.n] = ctas;
+    fold_batch_kernel<<<ctas, 256, smem, static_cast<cudaStream_t>(stream)>>>(b);
+    const int rc = launch_status();
+    if (rc) return rc;
+  }
+  return WDIT_OK;
 }
 
 int wdit_layernorm_modulation(const void* x, int x_is_bf16, int ldx, int M, int D, const float* scale,
@@ -467,6 +613,13 @@ int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, in
   rope_table_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(freqs_ri, max_pos, f, h, w, pair_major,
                                                                             cos_out, sin_out);
   return launch_status();
+}
+
+int wdit_rms_apply_layers(void* x, int ldx, int M, const float* part, int part_ld, int width, const float* w,
+                          float eps, int layers, long long x_layer_stride, int part_layer_stride, int w_layer_stride,
+                          void* stream) {
+  return launch_rms_apply_layers(x, ldx, M, part, part_ld, width, w, eps, layers, x_layer_stride, part_layer_stride,
+                                 w_layer_stride, stream);
 }
 
 }  // extern "C"

@@ -196,6 +196,7 @@ class FusedWanModel(nn.Module):
             blocks.append(fb)
         model.blocks = nn.ModuleList(blocks)
         self.dim = int(model.patch_embedding.weight.shape[0])
+        self.ckv_all = self._pack_cross_kv(blocks)
         self.patch = tuple(model.patch_embedding.kernel_size)
         self.out_dim = model.head.head.weight.shape[0] // math.prod(self.patch)
         self.freq_dim = model.time_embedding[0].weight.shape[1]
@@ -260,18 +261,74 @@ class FusedWanModel(nn.Module):
         c = ops.gemm_act(c, self.w_t2, vec=self.b_t2, act="none")
         return c.view(B, Lc, self.dim)
 
-    def head(self, x32, e, carry_stats, rows, shared_e: bool):
-        """LayerNorm + 2-vector modulation + Linear(dim -> prod(patch)*out_dim), LN absorbed."""
+    def _pack_cross_kv(self, blocks):
+        """Move every block's packed cross-attention K/V weight, bias and K-norm weight into one
+        allocation each (the blocks keep views), so one GEMM per forward projects the text
+        context for all blocks. None when the blocks do not share shapes and eps."""
         D = self.dim
-        xb, stats = carry_stats
+        if not blocks or any(b.w_ckv.shape != (2 * D, D) or b.rms_eps != blocks[0].rms_eps for b in blocks):
+            return None
+        L, dev = len(blocks), blocks[0].w_ckv.device
+        w_all = torch.empty((L * 2 * D, D), dtype=torch.bfloat16, device=dev)
+        b_all = torch.empty(L * 2 * D, dtype=torch.float32, device=dev)
+        wk_all = torch.empty((L, D), dtype=torch.float32, device=dev)
+        for i, blk in enumerate(blocks):
+            rows = slice(i * 2 * D, (i + 1) * 2 * D)
+            w_all[rows].copy_(blk.w_ckv)
+            b_all[rows].copy_(blk.b_ckv)
+            wk_all[i].copy_(blk.w_cnk)
+            blk.adopt_cross_kv(w_all[rows], b_all[rows], wk_all[i])
+        return w_all, b_all, wk_all, blocks[0].rms_eps
+
+    def cross_kv(self, context: torch.Tensor) -> None:
+        """Cross-attention K/V of every block for this forward's text context, in one GEMM and
+        one RMSNorm launch; each block takes its columns in its next forward."""
+        if self.ckv_all is None:
+            return
+        w_all, b_all, wk_all, eps = self.ckv_all
+        Bc, Lc, D = context.shape
+        kv = ops.cross_kv_layers(context.reshape(Bc * Lc, D), w_all, b_all, wk_all, eps)
+        for i, blk in enumerate(self.model.blocks):
+            blk.set_cross_kv(context, kv[:, i * 2 * D:(i + 1) * 2 * D])
+
+    def _head_fold_specs(self, e, shared_e: bool) -> list[dict]:
         e2 = e.float()
-        outs = []
         Be = 1 if shared_e else e2.shape[0]
+        return [dict(w=self.w_head, mult_c=1.0, mult_a=self.head_mod[1], mult_b=e2[b], shift_a=self.head_mod[0],
+                     shift_b=e2[b], bias=self.b_head) for b in range(Be)]
+
+    def prefold(self, e, e0, shared_e: bool) -> list:
+        """All adaLN weight folds of one forward step in one launch: every block's QKV and FFN1
+        folds (handed to the blocks for their next forward with this e0) and the head's fold
+        (returned). They depend only on the step's time embedding."""
+        specs, owners = [], []
+        for blk in self.model.blocks:
+            sp = blk.fold_specs(e0)
+            owners.append((blk, len(specs), len(sp)))
+            specs += sp
+        head_first = len(specs)
+        specs += self._head_fold_specs(e, shared_e)
+        folds = ops.fold_weight_batch(specs)
+        for blk, i0, n in owners:
+            blk.set_prefolded(e0, folds[i0:i0 + n])
+        return folds[head_first:]
+
+    def head(self, x32, e, carry_stats, rows, shared_e: bool, folds: list | None = None):
+        """LayerNorm + 2-vector modulation + Linear(dim -> prod(patch)*out_dim), LN absorbed.
+        `folds`: this head's weight folds from `prefold` (computed here when absent)."""
+        xb, stats = carry_stats
+        specs = self._head_fold_specs(e, shared_e)
+        Be = len(specs)
+        outs = []
         per = rows // Be
         for b in range(Be):
             r0, r1 = b * per, (b + 1) * per
-            wf, cs, vec = ops.fold_weight(self.w_head, mult_c=1.0, mult_a=self.head_mod[1], mult_b=e2[b],
-                                          shift_a=self.head_mod[0], shift_b=e2[b], bias=self.b_head)
+            if folds is not None and len(folds) == Be:
+                wf, cs, vec = folds[b]
+            else:
+                sp = specs[b]
+                wf, cs, vec = ops.fold_weight(sp["w"], mult_c=1.0, mult_a=sp["mult_a"], mult_b=sp["mult_b"],
+                                              shift_a=sp["shift_a"], shift_b=sp["shift_b"], bias=sp["bias"])
             outs.append(ops.gemm_act(xb[r0:r1], wf, vec=vec, act="none", ln=ops.LnFold(cs, stats[r0:r1], self.eps)))
         return torch.cat(outs) if len(outs) > 1 else outs[0]
 
@@ -301,7 +358,9 @@ class FusedWanModel(nn.Module):
         token_range = None if sp is None else (sp.token_offset, sp.token_offset + sp.local_len)
         x, grids, lens = self.embed_tokens(x_list, seq_len, token_range)
         e, e0 = self.embed_time(t[:1] if shared_e else t)
+        head_folds = self.prefold(e, e0, shared_e)
         context = self.embed_text(context_list, text_len)
+        self.cross_kv(context)
         Lx = x.shape[1]
         seq_lens = torch.tensor(lens, dtype=torch.long) if sp is None else None
         grid_sizes = torch.tensor(grids, dtype=torch.long)
@@ -314,7 +373,7 @@ class FusedWanModel(nn.Module):
             x = blk(x, e0, seq_lens_arg, grid_sizes, self.freqs, context, None)
         x32 = x.reshape(B * Lx, self.dim)
         carried = self.carry.get(x32)
-        y = self.head(x32, e, carried, B * Lx, shared_e)
+        y = self.head(x32, e, carried, B * Lx, shared_e, head_folds)
         if sp is not None or return_tokens:
             return y.view(B, Lx, -1)
         return [u.float() for u in self.unpatchify(y, grids, lens, Lx)]

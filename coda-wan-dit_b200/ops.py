@@ -4,7 +4,9 @@ Two layers:
 
 * Low-level fused GEMMs (``gemm_act``, ``gemm_residual``, ``gemm_norm``) and memory-bound
   passes (``ln_stats``, ``fold_weight``) with the full epilogue feature set; the drop-in
-  block uses these.
+  block uses these. The model adds two all-blocks forms: ``fold_weight_batch`` (every adaLN
+  weight fold of a step in one launch) and ``cross_kv_layers`` (every block's cross-attention
+  K/V in one GEMM).
 * The reference op API, same names / argument meaning / assertions as
   coda_wan/wan_coda_kernels.py and coda_wan/wan_gate_residual_coda.py:
   ``layernorm_modulation_bf16``, ``linear_bias_gelu_fixed``, ``qk_linear_bias_partial_rms``,
@@ -265,6 +267,51 @@ def fold_weight(w, *, mult_c, mult_a=None, mult_b=None, shift_a=None, shift_b=No
         ptr(bias), ptr(w_out), w_out.stride(0), ptr(csum_out), ptr(vec_out), stream_ptr(),
     )
     return w_out, csum_out, vec_out
+
+
+def cross_kv_layers(ctx: torch.Tensor, w_all: torch.Tensor, b_all: torch.Tensor, wk_all: torch.Tensor,
+                    eps: float) -> torch.Tensor:
+    """Cross-attention K and V of every block in one GEMM: ctx [M, D] bf16 times the blocks'
+    packed [K_l; V_l] weights w_all [L * 2D, D] (+ b_all), then the WanRMSNorm of each K_l with
+    weight wk_all[l] in one launch. Returns [M, L * 2D] bf16; block l's K and V are columns
+    [2Dl, 2Dl + D) and [2Dl + D, 2D(l + 1)). Same arithmetic as `gemm_norm` per block."""
+    L, D = wk_all.shape
+    M = ctx.shape[0]
+    N = w_all.shape[0]
+    assert N == 2 * D * L and w_all.shape[1] == D and b_all.numel() == N and wk_all.stride(1) == 1
+    part = torch.empty((M, N // RMS_BLOCK), dtype=torch.float32, device=ctx.device)
+    out = gemm_act(ctx, w_all, vec=b_all, ms_out=part, ms_cols=N)
+    call("wdit_rms_apply_layers", ptr(out), out.stride(0), M, ptr(part), part.stride(0), D, ptr(wk_all),
+         float(eps), L, 2 * D, 2 * D // RMS_BLOCK, wk_all.stride(0), stream_ptr())
+    return out
+
+
+def fold_weight_batch(specs: list[dict]) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+    """Many `fold_weight` calls in one launch. Each spec holds fold_weight's arguments
+    (`w`, `mult_c`, optional `mult_a`, `mult_b`, `shift_a`, `shift_b`, `bias`); returns the
+    (w_out, csum, vec) triple of each spec, in order."""
+    if not specs:
+        return []
+    jobs = (_lib.FoldJob * len(specs))()
+    outs, keep = [], []
+    for j, sp in zip(jobs, specs):
+        w = sp["w"]
+        _require_cuda(w)
+        N, K = w.shape
+        assert w.stride(1) == 1 and w.dtype == torch.bfloat16
+        w_out = torch.empty((N, K), dtype=torch.bfloat16, device=w.device)
+        csum = torch.empty(N, dtype=torch.float32, device=w.device)
+        vec = torch.empty(N, dtype=torch.float32, device=w.device)
+        bias = _f32vec(sp.get("bias"))
+        keep.append(bias)
+        j.W, j.ldw, j.N, j.K, j.mult_c = ptr(w), w.stride(0), N, K, float(sp["mult_c"])
+        j.mult_a, j.mult_b = ptr(sp.get("mult_a")), ptr(sp.get("mult_b"))
+        j.shift_a, j.shift_b, j.bias = ptr(sp.get("shift_a")), ptr(sp.get("shift_b")), ptr(bias)
+        j.W_out, j.ldw_out, j.csum_out, j.vec_out = ptr(w_out), w_out.stride(0), ptr(csum), ptr(vec)
+        outs.append((w_out, csum, vec))
+    launches = -(-len(specs) // _lib.FOLD_JOBS_PER_LAUNCH)
+    call("wdit_fold_weight_batch", jobs, len(specs), stream_ptr(), kernels=launches)
+    return outs
 
 
 # ---------------------------------------------------------------------------

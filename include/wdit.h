@@ -173,6 +173,32 @@ int wdit_fold_weight(const void* W, int ldw, int N, int K, float mult_c, const f
                      float* csum_out, float* vec_out, void* stream);
 
 /*
+ * Many wdit_fold_weight calls in one launch (up to 64 per launch; more are split): all of a
+ * forward step's adaLN folds (every block's QKV and FFN1 weights and the head) at once, since
+ * they depend only on the step's time embedding. Each job has wdit_fold_weight's arguments
+ * and checks; the first failing job's status is returned before anything is launched.
+ * Replaces: the per-block modulation at coda_wan/run_wan_coda.py:142 and
+ * coda_wan/wan_coda_kernels.py:52-55, for all blocks of a step.
+ */
+typedef struct wdit_fold_job {
+  const void* W;
+  int ldw;
+  int N;
+  int K;
+  float mult_c;
+  const float* mult_a;
+  const float* mult_b;
+  const float* shift_a;
+  const float* shift_b;
+  const float* bias;
+  void* W_out;
+  int ldw_out;
+  float* csum_out;
+  float* vec_out;
+} wdit_fold_job;
+int wdit_fold_weight_batch(const wdit_fold_job* jobs, int n_jobs, void* stream);
+
+/*
  * out[M,D] (bf16) = (x - mean) * rsqrt(var + eps) * (1 + scale) + shift, x fp32 or bf16.
  * Replaces: coda_wan/wan_coda_kernels.py:59-81 layernorm_modulation_bf16.
  */
@@ -184,6 +210,20 @@ int wdit_layernorm_modulation(const void* x, int x_is_bf16, int ldx, int M, int 
  * Replaces: coda_wan/wan_coda_kernels.py:392-411 rmsnorm_fused.
  */
 int wdit_rmsnorm(const void* x, int ldx, int M, int D, const float* w, float eps, void* out, int ldo, void* stream);
+
+/*
+ * In-place WanRMSNorm of `layers` column groups of x[M, ldx] (bf16) from the per-128-column
+ * mean-square partials that wdit_gemm_act writes (ms_out): group l is columns
+ * [l * x_layer_stride, l * x_layer_stride + width) of every row, its partials start at column
+ * l * part_layer_stride of part[M, part_ld] and its weight at w + l * w_layer_stride (fp32).
+ * Normalizes the cross-attention K of every block after one GEMM projected the text context
+ * through all blocks' packed K/V weights. width % 128 == 0; strides in elements.
+ * Replaces: coda_wan/wan_coda_kernels.py:371-411 rmsnorm_fused applied to the cross-attention
+ * k of each block (coda_wan/run_wan_coda.py:179-182).
+ */
+int wdit_rms_apply_layers(void* x, int ldx, int M, const float* part, int part_ld, int width, const float* w,
+                          float eps, int layers, long long x_layer_stride, int part_layer_stride, int w_layer_stride,
+                          void* stream);
 
 /*
  * In-place WanRMSNorm + RoPE of q and k from per-128-column mean-square partials.

@@ -86,3 +86,25 @@ def test_p2p_argument_validation_without_device(lib):
     assert lib.wdit_p2p_wait(dummy, 0, 1, null) == 2
     assert lib.wdit_ipc_handle(null, null, None) == 1
     assert lib.wdit_ipc_open(null, None) == 1
+
+
+def test_batched_entry_points_validate_without_device(lib, pkg):
+    null = ctypes.c_void_p(None)
+    dummy = ctypes.c_void_p(0x1000)
+    # rms_apply_layers: null operands, no layers, last layer past the row, misaligned layer stride
+    assert lib.wdit_rms_apply_layers(null, 9216, 4, dummy, 72, 1536, dummy, 1e-6, 3, 3072, 24, 1536, null) == 1
+    assert lib.wdit_rms_apply_layers(dummy, 9216, 4, dummy, 72, 1536, dummy, 1e-6, 0, 3072, 24, 1536, null) == 2
+    assert lib.wdit_rms_apply_layers(dummy, 9216, 4, dummy, 72, 1536, dummy, 1e-6, 4, 3072, 24, 1536, null) == 2
+    assert lib.wdit_rms_apply_layers(dummy, 9216, 4, dummy, 59, 1536, dummy, 1e-6, 3, 3072, 24, 1536, null) == 2
+    assert lib.wdit_rms_apply_layers(dummy, 9216, 4, dummy, 72, 1536, dummy, 1e-6, 2, 3076, 24, 1536, null) == 3
+    # fold batch: negative count, a job with K % 8 != 0, a null output
+    jobs = (pkg._lib.FoldJob * 2)()
+    for j in jobs:
+        j.W, j.ldw, j.N, j.K, j.mult_c = 0x1000, 64, 4, 64, 1.0
+        j.W_out, j.ldw_out, j.csum_out, j.vec_out = 0x2000, 64, 0x3000, 0x4000
+    assert lib.wdit_fold_weight_batch(jobs, -1, null) == 1
+    jobs[1].K = 60
+    assert lib.wdit_fold_weight_batch(jobs, 2, null) == 2
+    jobs[1].K, jobs[1].W_out = 64, None
+    assert lib.wdit_fold_weight_batch(jobs, 2, null) == 1
+    assert lib.wdit_fold_weight_batch(jobs, 0, null) == 0

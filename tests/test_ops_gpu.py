@@ -73,6 +73,48 @@ def test_gemm_act_layernorm_fold(pkg, offset):
     assert rel_l2(got, want) < tol
 
 
+def test_cross_kv_layers(pkg):
+    """All blocks' cross-attention K/V in one GEMM + one RMSNorm launch equals gemm_norm per block."""
+    L, D, M = 3, 1536, 300
+    ctx = rand((M, D), seed=700)
+    ws = [rand((2 * D, D), 0.02, seed=701 + i) for i in range(L)]
+    bs = [rand((2 * D,), 0.01, seed=711 + i, dtype=torch.float32) for i in range(L)]
+    wks = [1.0 + rand((D,), 0.1, seed=721 + i, dtype=torch.float32) for i in range(L)]
+    got = pkg.ops.cross_kv_layers(ctx, torch.cat(ws), torch.cat(bs), torch.stack(wks), 1e-6)
+    assert got.shape == (M, 2 * D * L)
+    for i in range(L):
+        want = pkg.ops.gemm_norm(ctx, ws[i], vec=bs[i], norm_groups=1, norm_width=D, norm_w=(wks[i], None),
+                                 norm_eps=1e-6)
+        assert torch.equal(got[:, 2 * D * i:2 * D * (i + 1)], want)
+
+
+def test_fold_weight_batch(pkg):
+    """One launch of many folds equals the single-fold kernel bit for bit, for ragged N and K,
+    absent vectors and more jobs than one launch holds (64)."""
+    shapes = [(4608, 1536), (8960, 1536), (100, 1536), (64, 5120), (7, 8)] * 14  # 70 jobs: two launches
+    specs = []
+    for i, (N, K) in enumerate(shapes):
+        sp = dict(w=rand((N, K), 0.02, seed=100 + i), mult_c=1.0 if i % 3 else 0.0,
+                  mult_a=rand((K,), 0.1, seed=200 + i, dtype=torch.float32))
+        if i % 2 == 0:
+            sp.update(mult_b=rand((K,), 0.1, seed=300 + i, dtype=torch.float32),
+                      shift_a=rand((K,), 0.1, seed=400 + i, dtype=torch.float32),
+                      shift_b=rand((K,), 0.1, seed=500 + i, dtype=torch.float32))
+        if i % 4 != 3:
+            sp["bias"] = rand((N,), 0.01, seed=600 + i, dtype=torch.float32)
+        specs.append(sp)
+    got = pkg.ops.fold_weight_batch(specs)
+    assert len(got) == len(specs)
+    for sp, (wf, cs, vec) in zip(specs, got):
+        want = pkg.ops.fold_weight(sp["w"], mult_c=sp["mult_c"], mult_a=sp.get("mult_a"), mult_b=sp.get("mult_b"),
+                                   shift_a=sp.get("shift_a"), shift_b=sp.get("shift_b"), bias=sp.get("bias"))
+        assert torch.equal(wf, want[0]) and torch.equal(cs, want[1]) and torch.equal(vec, want[2])
+    assert pkg.ops.fold_weight_batch([]) == []
+    bad = dict(specs[0], w=rand((16, 12), 0.02, seed=7))  # K % 8 != 0
+    with pytest.raises(RuntimeError, match="unsupported shape"):
+        pkg.ops.fold_weight_batch([specs[1], bad])
+
+
 @pytest.mark.parametrize("M,N,K,gate,inplace", [(129, 1536, 1536, True, True), (4095, 1536, 8960, True, False),
                                                 (300, 512, 256, False, True), (1, 256, 64, True, True),
                                                 (777, 64, 512, True, False), (777, 320, 512, True, True),

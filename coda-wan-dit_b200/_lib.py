@@ -70,6 +70,7 @@ _SIGNATURES = {
     "wdit_rmsnorm": (c_int, [P, I, I, I, P, F, P, I, P]),
     "wdit_qk_rms_rope_from_partials": (c_int, [P, I, P, I, I, P, P, P, P, F, P]),
     "wdit_rms_apply_layers": (c_int, [P, I, I, P, I, I, P, F, I, c_longlong, I, I, P]),
+    "wdit_patch_rows": (c_int, [P, I, I, I, I, I, I, I, c_longlong, I, I, P, P]),
     "wdit_rope_table": (c_int, [P, I, I, I, I, I, P, P, P]),
     "wdit_ulysses_pack": (c_int, [P, I, I, I, I, I, I, I, P, P]),
     "wdit_seq_gather": (c_int, [P, I, I, I, I, I, P, P]),
@@ -139,7 +140,7 @@ def check(rc: int, what: str) -> None:
 # Entry points that launch device work (counted by launch_counter for the benchmark).
 _LAUNCHING = {
     "wdit_gemm_act", "wdit_gemm_residual", "wdit_gemm_norm", "wdit_ln_stats", "wdit_fold_weight",
-    "wdit_fold_weight_batch", "wdit_rms_apply_layers",
+    "wdit_fold_weight_batch", "wdit_rms_apply_layers", "wdit_patch_rows",
     "wdit_layernorm_modulation", "wdit_rmsnorm", "wdit_qk_rms_rope_from_partials", "wdit_rope_table",
     "wdit_ulysses_pack", "wdit_seq_gather", "wdit_seq_scatter", "wdit_ulysses_unpack",
     "wdit_p2p_qkv_exchange", "wdit_p2p_out_exchange", "wdit_p2p_wait",

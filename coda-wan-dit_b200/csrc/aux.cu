@@ -12,6 +12,8 @@
 //                        the second half of every norm GEMM and the reference op
 //                        coda_wan/wan_coda_kernels.py:233-352.
 //   rope_table_kernel    reference op coda_wan/wan_coda_kernels.py:414-430.
+//   patch_rows_kernel    im2col of the non-overlapping patch embedding (the Conv3d becomes a
+//                        GEMM with the bias in its epilogue).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -397,6 +399,43 @@ __global__ void __launch_bounds__(32 * kApplyRowsPerBlock)
 }
 
 // ---------------------------------------------------------------------------
+// Patch rows of one latent u[C, F, H, W] (bf16) for a non-overlapping patch (pt, ph, pw):
+// row r is token t = tok_lo + r of the (F/pt, H/ph, W/pw) grid (frame-major), column
+// k = ((c * pt + kt) * ph + kh) * pw + kw holds u[c, f pt + kt, i ph + kh, j pw + kw], i.e. the
+// Conv3d weight [D, C, pt, ph, pw] flattened to [D, K] is the GEMM's B operand. Columns K..Kp-1
+// and tokens past the grid are zero. One thread per 8 columns (one 16-byte store).
+__global__ void __launch_bounds__(256)
+    patch_rows_kernel(const __nv_bfloat16* __restrict__ u, int C, int F, int H, int W, int pt, int ph, int pw,
+                      long long tok_lo, int rows, int K, int Kp, __nv_bfloat16* __restrict__ out) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int groups = Kp / 8;
+  if (idx >= static_cast<long long>(rows) * groups) return;
+  const int row = static_cast<int>(idx / groups);
+  const int k0 = static_cast<int>(idx - static_cast<long long>(row) * groups) * 8;
+  const int Fp = F / pt, Hp = H / ph, Wp = W / pw;
+  const long long ntok = static_cast<long long>(Fp) * Hp * Wp;
+  const long long t = tok_lo + row;
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  if (t < ntok) {
+    const int f = static_cast<int>(t / (static_cast<long long>(Hp) * Wp));
+    const int rem = static_cast<int>(t - static_cast<long long>(f) * Hp * Wp);
+    const int hi = rem / Wp, wi = rem - (rem / Wp) * Wp;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int k = k0 + i;
+      if (k < K) {
+        const int kw = k % pw, kh = (k / pw) % ph, kt = (k / (pw * ph)) % pt, c = k / (pw * ph * pt);
+        const size_t src = ((static_cast<size_t>(c) * F + f * pt + kt) * H + hi * ph + kh) * W + wi * pw + kw;
+        v[i] = __bfloat162float(u[src]);
+      }
+    }
+  }
+  store8_bf16(out, static_cast<size_t>(row) * Kp + k0, v);
+}
+
+// ---------------------------------------------------------------------------
 __global__ void rope_table_kernel(const double* __restrict__ freqs_ri, int max_pos, int f, int h, int w,
                                   int pair_major, float* __restrict__ cos_out, float* __restrict__ sin_out) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -612,6 +651,22 @@ int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, in
   const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
   rope_table_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(freqs_ri, max_pos, f, h, w, pair_major,
                                                                             cos_out, sin_out);
+  return launch_status();
+}
+
+int wdit_patch_rows(const void* latent, int C, int F, int H, int W, int pt, int ph, int pw, long long token_lo,
+                    int rows, int Kp, void* out, void* stream) {
+  if (latent == nullptr || out == nullptr) return WDIT_ERR_ARG;
+  if (C <= 0 || pt <= 0 || ph <= 0 || pw <= 0 || F < pt || H < ph || W < pw || rows <= 0 || token_lo < 0)
+    return WDIT_ERR_SHAPE;
+  const int K = C * pt * ph * pw;
+  if (Kp < K || Kp % 8 != 0) return WDIT_ERR_SHAPE;
+  if (!a16(out)) return WDIT_ERR_ALIGN;
+  const long long total = static_cast<long long>(rows) * (Kp / 8);
+  const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+  patch_rows_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(latent), C, F, H, W, pt, ph, pw, token_lo, rows, K, Kp,
+      reinterpret_cast<__nv_bfloat16*>(out));
   return launch_status();
 }
 

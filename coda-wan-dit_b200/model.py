@@ -198,6 +198,15 @@ class FusedWanModel(nn.Module):
         self.dim = int(model.patch_embedding.weight.shape[0])
         self.ckv_all = self._pack_cross_kv(blocks)
         self.patch = tuple(model.patch_embedding.kernel_size)
+        # Patch embedding as a GEMM: the Conv3d weight [D, C, pt, ph, pw] flattened to [D, K],
+        # K zero-padded to a multiple of 64 (the GEMM's K step); patch_rows builds the A operand.
+        pe = model.patch_embedding
+        assert tuple(pe.stride) == self.patch, "patch embedding with stride != kernel size"
+        wk = pe.weight.detach().reshape(self.dim, -1)
+        kp = -(-wk.shape[1] // 64) * 64
+        self.w_patch = torch.zeros((self.dim, kp), dtype=torch.bfloat16, device=wk.device)
+        self.w_patch[:, :wk.shape[1]] = wk.to(torch.bfloat16)
+        self.b_patch = pe.bias.detach().float().contiguous()
         self.out_dim = model.head.head.weight.shape[0] // math.prod(self.patch)
         self.freq_dim = model.time_embedding[0].weight.shape[1]
         te = model.text_embedding
@@ -220,34 +229,32 @@ class FusedWanModel(nn.Module):
 
     # -- embeddings --------------------------------------------------------
     def embed_tokens(self, x_list, seq_len, token_range: tuple[int, int] | None = None):
-        """Patch embedding -> [B, seq_len, dim] bf16 (zero-padded), grids, true lengths.
+        """Patch embedding -> [B, rows, dim] bf16 (tokens past a sample's grid are zero), grids,
+        true lengths. The Conv3d (kernel = stride = patch) runs as patch rows + one GEMM with the
+        bias in its epilogue.
 
-        token_range (lo, hi): embed only tokens [lo, hi) of every sample (a token shard); only the
-        latent frames that hold them go through the convolution."""
-        pe = self.model.patch_embedding
-        w = pe.weight.to(torch.bfloat16)
-        b = pe.bias.to(torch.bfloat16)
+        token_range (lo, hi): embed only tokens [lo, hi) of every sample (a token shard)."""
+        lo, hi = token_range if token_range is not None else (0, seq_len)
+        rows, B, D = hi - lo, len(x_list), self.dim
         pt, ph, pw = self.patch
-        grids, lens, xs = [], [], []
-        for u in x_list:
+        dev = self.w_patch.device
+        grids, lens = [], []
+        pr = torch.empty((B * rows, self.w_patch.shape[1]), dtype=torch.bfloat16, device=dev)
+        for b, u in enumerate(x_list):
             g = (u.shape[1] // pt, u.shape[2] // ph, u.shape[3] // pw)
             grids.append(g)
             lens.append(g[0] * g[1] * g[2])
-            if token_range is None:
-                v = F.conv3d(u.unsqueeze(0).to(torch.bfloat16), w, b, stride=self.patch)
-                xs.append(F.pad(v.flatten(2).transpose(1, 2), (0, 0, 0, seq_len - lens[-1])))
-                continue
-            lo, hi = token_range
-            per_frame = g[1] * g[2]
-            f0 = min(lo // per_frame, g[0])
-            f1 = min(-(-hi // per_frame), g[0])
-            if f1 > f0:
-                v = F.conv3d(u[:, f0 * pt:f1 * pt].unsqueeze(0).to(torch.bfloat16), w, b, stride=self.patch)
-                v = v.flatten(2).transpose(1, 2)[:, lo - f0 * per_frame:hi - f0 * per_frame]
-            else:
-                v = torch.zeros((1, 0, self.dim), dtype=torch.bfloat16, device=u.device)
-            xs.append(F.pad(v, (0, 0, 0, (hi - lo) - v.shape[1])))  # tokens past the sample's end are zero
-        return torch.cat(xs), grids, lens
+            ops.patch_rows(u, self.patch, lo, rows, pr.shape[1], out=pr[b * rows:(b + 1) * rows])
+        x = torch.empty((B, rows, D), dtype=torch.bfloat16, device=dev)
+        valid = [max(0, min(n - lo, rows)) for n in lens]
+        if all(v == rows for v in valid):
+            ops.gemm_act(pr, self.w_patch, vec=self.b_patch, out=x.view(B * rows, D))
+        else:
+            for b, v in enumerate(valid):
+                if v > 0:
+                    ops.gemm_act(pr[b * rows:b * rows + v], self.w_patch, vec=self.b_patch, out=x[b, :v])
+                x[b, v:].zero_()
+        return x, grids, lens
 
     def embed_time(self, t: torch.Tensor):
         e = self.model.time_embedding(sinusoidal_embedding(self.freq_dim, t).float())

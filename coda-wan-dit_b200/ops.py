@@ -269,6 +269,20 @@ def fold_weight(w, *, mult_c, mult_a=None, mult_b=None, shift_a=None, shift_b=No
     return w_out, csum_out, vec_out
 
 
+def patch_rows(latent: torch.Tensor, patch: tuple[int, int, int], token_lo: int, rows: int, Kp: int,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Patch-embedding rows of latent [C, F, H, W]: out [rows, Kp] bf16, row r = the flattened
+    (c, kt, kh, kw) patch of token token_lo + r (zero past the grid and past K columns)."""
+    _require_cuda(latent)
+    u = latent.to(torch.bfloat16).contiguous()
+    C, F_, H, W = u.shape
+    if out is None:
+        out = torch.empty((rows, Kp), dtype=torch.bfloat16, device=u.device)
+    assert out.shape == (rows, Kp) and out.is_contiguous() and out.dtype == torch.bfloat16
+    call("wdit_patch_rows", ptr(u), C, F_, H, W, *patch, int(token_lo), rows, Kp, ptr(out), stream_ptr())
+    return out
+
+
 def cross_kv_layers(ctx: torch.Tensor, w_all: torch.Tensor, b_all: torch.Tensor, wk_all: torch.Tensor,
                     eps: float) -> torch.Tensor:
     """Cross-attention K and V of every block in one GEMM: ctx [M, D] bf16 times the blocks'

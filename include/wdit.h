@@ -212,6 +212,18 @@ int wdit_layernorm_modulation(const void* x, int x_is_bf16, int ldx, int M, int 
 int wdit_rmsnorm(const void* x, int ldx, int M, int D, const float* w, float eps, void* out, int ldo, void* stream);
 
 /*
+ * Patch rows for the patch embedding as a GEMM: latent[C, F, H, W] (bf16, contiguous), patch
+ * (pt, ph, pw) with stride = patch; out[rows, Kp] (bf16) row r = the patch of token
+ * token_lo + r of the (F/pt, H/ph, W/pw) grid (frame-major), column ((c*pt + kt)*ph + kh)*pw + kw,
+ * K = C*pt*ph*pw <= Kp (Kp % 8 == 0); columns past K and tokens past the grid are zero.
+ * out . weight.reshape(D, K)^T + bias (wdit_gemm_act, K padded to Kp) is the Conv3d.
+ * Replaces: the Conv3d patch embedding of the stock Wan forward the reference calls at
+ * coda_wan/run_wan_coda.py:250 (nn.Conv3d with kernel = stride = patch_size).
+ */
+int wdit_patch_rows(const void* latent, int C, int F, int H, int W, int pt, int ph, int pw, long long token_lo,
+                    int rows, int Kp, void* out, void* stream);
+
+/*
  * In-place WanRMSNorm of `layers` column groups of x[M, ldx] (bf16) from the per-128-column
  * mean-square partials that wdit_gemm_act writes (ms_out): group l is columns
  * [l * x_layer_stride, l * x_layer_stride + width) of every row, its partials start at column

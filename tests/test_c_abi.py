@@ -108,3 +108,12 @@ def test_batched_entry_points_validate_without_device(lib, pkg):
     jobs[1].K, jobs[1].W_out = 64, None
     assert lib.wdit_fold_weight_batch(jobs, 2, null) == 1
     assert lib.wdit_fold_weight_batch(jobs, 0, null) == 0
+
+
+def test_patch_rows_validates_without_device(lib):
+    null = ctypes.c_void_p(None)
+    dummy = ctypes.c_void_p(0x1000)
+    assert lib.wdit_patch_rows(null, 16, 21, 60, 104, 1, 2, 2, 0, 32760, 64, dummy, null) == 1
+    assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 32760, 56, dummy, null) == 2  # Kp < K
+    assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 0, 64, dummy, null) == 2      # no rows
+    assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 32760, 64, ctypes.c_void_p(0x1008), null) == 3

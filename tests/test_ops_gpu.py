@@ -73,6 +73,29 @@ def test_gemm_act_layernorm_fold(pkg, offset):
     assert rel_l2(got, want) < tol
 
 
+@pytest.mark.parametrize("patch,shape,lo,rows", [((1, 2, 2), (16, 3, 8, 12), 0, 72), ((1, 2, 2), (16, 3, 8, 12), 20, 64),
+                                                  ((2, 2, 2), (36, 4, 6, 8), 5, 40)])
+def test_patch_embedding_as_gemm(pkg, patch, shape, lo, rows):
+    """patch_rows + gemm_act (bias epilogue) is the stride = kernel Conv3d of the stock patch
+    embedding; rows past the grid are zero patch rows (K padded to a multiple of 64)."""
+    C, D = shape[0], 256
+    u = rand(shape, 1.0, seed=800, dtype=torch.float32)
+    w = rand((D, C) + patch, 0.05, seed=801)
+    b = rand((D,), 0.1, seed=802, dtype=torch.float32)
+    K = C * patch[0] * patch[1] * patch[2]
+    Kp = -(-K // 64) * 64
+    pr = pkg.ops.patch_rows(u, patch, lo, rows, Kp)
+    wp = torch.zeros((D, Kp), dtype=torch.bfloat16, device=DEV)
+    wp[:, :K] = w.reshape(D, K)
+    got = pkg.ops.gemm_act(pr, wp, vec=b)
+    ref = torch.nn.functional.conv3d(u.to(torch.bfloat16).float()[None], w.float(), b, stride=patch)[0]
+    ref = ref.flatten(1).t()  # [tokens, D], frame-major
+    valid = max(0, min(ref.shape[0] - lo, rows))
+    assert valid > 0
+    assert rel_l2(got[:valid], ref[lo:lo + valid]) < 1e-2
+    assert torch.count_nonzero(pr[valid:]) == 0 and torch.count_nonzero(pr[:, K:]) == 0
+
+
 def test_cross_kv_layers(pkg):
     """All blocks' cross-attention K/V in one GEMM + one RMSNorm launch equals gemm_norm per block."""
     L, D, M = 3, 1536, 300

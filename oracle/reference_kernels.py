@@ -15,7 +15,8 @@ import sys
 import types
 from pathlib import Path
 
-REFERENCE_DIR = Path(os.environ.get("WDIT_REFERENCE_DIR", "/root/reference"))
+# Root of a checkout of the reference (the directory holding coda_wan/), from the environment.
+REFERENCE_DIR = Path(os.environ["WDIT_REFERENCE_DIR"]) if os.environ.get("WDIT_REFERENCE_DIR") else None
 
 _STUB_MODULES = [
     "rapier",
@@ -43,13 +44,14 @@ class _InertEVT:
 
 
 def available() -> bool:
-    return (REFERENCE_DIR / "coda_wan" / "wan_coda_kernels.py").is_file()
+    return REFERENCE_DIR is not None and (REFERENCE_DIR / "coda_wan" / "wan_coda_kernels.py").is_file()
 
 
 def load():
     """Return the reference module `wan_coda_kernels` (Triton in interpreter mode)."""
     if not available():
-        raise FileNotFoundError(f"reference sources not found under {REFERENCE_DIR}")
+        raise FileNotFoundError("reference sources not found: set WDIT_REFERENCE_DIR to a checkout of "
+                                f"Owen718/CODA-Wan-DiT (now: {REFERENCE_DIR})")
     if "triton" in sys.modules and os.environ.get("TRITON_INTERPRET") != "1":
         raise RuntimeError("set TRITON_INTERPRET=1 before triton is imported")
     os.environ["TRITON_INTERPRET"] = "1"

@@ -1,7 +1,7 @@
 """CPU restatement of the sequence-parallel regrouping (test infrastructure only).
 
-The reference is single-GPU (no collectives anywhere, SURVEY.md-level finding recorded in
-DESIGN.md), so this is the oracle for the build's own token-sharded forward: rank r owns
+The reference is single-GPU (it has no collectives anywhere), so this is the oracle for the
+build's own token-sharded forward: rank r owns
 tokens [r*Lp, (r+1)*Lp) of each batch entry; the B*H (batch, head) units u = b*H + h are
 dealt out U = B*H/P per rank (unit u on rank u // U). These functions state the four layout
 maps with plain tensor indexing; the CUDA kernels (wdit_ulysses_pack / seq_gather /

@@ -1,6 +1,6 @@
 """Generate tests/golden/*.npz from the reference's own code (run in the build container).
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    WDIT_REFERENCE_DIR=<checkout of Owen718/CODA-Wan-DiT> TRITON_INTERPRET=1 python tests/golden/make_golden.py
 
 Sources (Owen718/CODA-Wan-DiT, imported through oracle/reference_kernels.py):
   ln_mod.npz      _layernorm_modulation_kernel via layernorm_modulation_bf16 (wan_coda_kernels.py:35-81)

@@ -117,3 +117,25 @@ def test_patch_rows_validates_without_device(lib):
     assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 32760, 56, dummy, null) == 2  # Kp < K
     assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 0, 64, dummy, null) == 2      # no rows
     assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 32760, 64, ctypes.c_void_p(0x1008), null) == 3
+
+
+def test_fold_job_struct_matches_header(pkg, tmp_path):
+    """The ctypes mirror of struct wdit_fold_job has the C layout (size and every offset)."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f for f, _ in pkg._lib.FoldJob._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text(
+        "#include <stddef.h>\n#include <stdio.h>\n#include \"wdit.h\"\nint main(void) {\n"
+        "  printf(\"%zu\\n\", sizeof(wdit_fold_job));\n"
+        + "".join(f"  printf(\"%zu\\n\", offsetof(wdit_fold_job, {f}));\n" for f in fields)
+        + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    want = [ctypes.sizeof(pkg._lib.FoldJob)] + [getattr(pkg._lib.FoldJob, f).offset for f in fields]
+    assert got == want

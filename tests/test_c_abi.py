@@ -139,3 +139,32 @@ def test_fold_job_struct_matches_header(pkg, tmp_path):
     got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
     want = [ctypes.sizeof(pkg._lib.FoldJob)] + [getattr(pkg._lib.FoldJob, f).offset for f in fields]
     assert got == want
+
+
+def _ctype_of(decl: str):
+    """ctypes class expected for one C parameter / return type of include/wdit.h."""
+    t = re.sub(r"\bconst\b", "", decl).strip()
+    if "*" in t:
+        return "pointer"
+    t = re.sub(r"\s+[A-Za-z_][A-Za-z0-9_]*$", "", t).strip() if " " in t else t  # drop the name
+    return {"int": ctypes.c_int, "float": ctypes.c_float, "long long": ctypes.c_longlong,
+            "unsigned int": ctypes.c_uint, "unsigned long long": ctypes.c_ulonglong}[t]
+
+
+def test_binding_signatures_match_the_header(pkg):
+    """Every prototype's return and argument types agree with the ctypes table (count and kind)."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    protos = re.findall(r"\b(int|long long)\s+(wdit_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text)
+    assert len(protos) == len(declared_symbols())
+    sigs = pkg._lib._SIGNATURES
+    for ret, name, params in protos:
+        res, args = sigs[name]
+        assert res == {"int": ctypes.c_int, "long long": ctypes.c_longlong}[ret], name
+        params = [p.strip() for p in params.split(",")] if params.strip() not in ("", "void") else []
+        assert len(params) == len(args), f"{name}: {len(params)} C parameters, {len(args)} in the binding"
+        for i, (p, a) in enumerate(zip(params, args)):
+            want = _ctype_of(p)
+            if want == "pointer":
+                assert a is ctypes.c_void_p or issubclass(a, ctypes._Pointer), f"{name} arg {i}: {p}"
+            else:
+                assert a is want, f"{name} arg {i}: {p} vs {a}"

@@ -469,6 +469,7 @@ inline unsigned row_blocks(int rows) { return static_cast<unsigned>((rows + kRow
 int launch_rms_rope_apply(void* x, int ldx, int M, const float* part, int part_ld, int groups, int width,
                           const float* w0, const float* w1, float eps, int rope_groups, const float* rope_cos,
                           const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (x == nullptr || part == nullptr || w0 == nullptr || (groups > 1 && w1 == nullptr)) return WDIT_ERR_ARG;
   if (M <= 0 || groups < 1 || groups > 2 || width <= 0 || width % 128 != 0 || ldx < groups * width) return WDIT_ERR_SHAPE;
   if (part_ld < groups * (width / 128)) return WDIT_ERR_SHAPE;
@@ -488,6 +489,7 @@ int launch_rms_rope_apply(void* x, int ldx, int M, const float* part, int part_l
 int launch_rms_apply_layers(void* x, int ldx, int M, const float* part, int part_ld, int width, const float* w,
                             float eps, int layers, long long x_layer_stride, int part_layer_stride, int w_layer_stride,
                             void* stream) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (x == nullptr || part == nullptr || w == nullptr) return WDIT_ERR_ARG;
   if (M <= 0 || width <= 0 || width % 128 != 0 || layers < 1 || layers > 65535) return WDIT_ERR_SHAPE;
   if (x_layer_stride < 0 || part_layer_stride < 0 || w_layer_stride < 0) return WDIT_ERR_SHAPE;
@@ -508,6 +510,7 @@ using namespace wdit;
 
 namespace {
 int fold_job_check(const wdit_fold_job& j) {
+  if (j.N == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (j.W == nullptr || j.W_out == nullptr || j.csum_out == nullptr || j.vec_out == nullptr) return WDIT_ERR_ARG;
   if (j.N <= 0 || j.K <= 0 || j.K % 8 != 0 || j.ldw < j.K || j.ldw_out < j.K) return WDIT_ERR_SHAPE;
   if (!a16(j.W) || !a16(j.W_out) || j.ldw % 8 != 0 || j.ldw_out % 8 != 0) return WDIT_ERR_ALIGN;
@@ -554,6 +557,7 @@ extern "C" {
 
 int wdit_ln_stats(const void* x, int x_is_bf16, int ldx, int M, int D, float* stats_out, void* x_bf16_out,
                   float* x_f32_out, void* stream) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (x == nullptr || stats_out == nullptr) return WDIT_ERR_ARG;
   if (M <= 0 || D <= 0 || D % 8 != 0 || ldx < D) return WDIT_ERR_SHAPE;
   if (!a16(x) || ldx % 8 != 0 || (reinterpret_cast<uintptr_t>(stats_out) & 7) != 0) return WDIT_ERR_ALIGN;
@@ -570,7 +574,7 @@ int wdit_fold_weight(const void* W, int ldw, int N, int K, float mult_c, const f
   const wdit_fold_job j = {W, ldw, N, K, mult_c, mult_a, mult_b, shift_a, shift_b, bias, W_out, ldw_out, csum_out,
                            vec_out};
   const int rc = fold_job_check(j);
-  if (rc) return rc;
+  if (rc || N == 0) return rc;
   const size_t smem = static_cast<size_t>(K) * 2 * sizeof(float);
   static bool attr_set[64] = {};
   allow_fold_smem(fold_weight_kernel, smem, attr_set);
@@ -589,7 +593,7 @@ int wdit_fold_weight_batch(const wdit_fold_job* jobs, int n_jobs, void* stream) 
   for (int i = 0; i < n_jobs; ++i) {
     const int rc = fold_job_check(jobs[i]);
     if (rc) return rc;
-    if (jobs[i].K > max_k) max_k = jobs[i].K;
+    if (jobs[i].N > 0 && jobs[i].K > max_k) max_k = jobs[i].K;
   }
   const size_t smem = static_cast<size_t>(max_k) * 2 * sizeof(float);
   static bool attr_set[64] = {};
@@ -604,6 +608,7 @@ int wdit_fold_weight_batch(const wdit_fold_job* jobs, int n_jobs, void* stream) 
       ctas += (jobs[j0 + i].N + kFoldRowsPerCta - 1) / kFoldRowsPerCta;
     }
     b.first[b.n] = ctas;
+    if (ctas == 0) continue;  // only empty jobs in this group
     fold_batch_kernel<<<ctas, 256, smem, static_cast<cudaStream_t>(stream)>>>(b);
     const int rc = launch_status();
     if (rc) return rc;
@@ -613,6 +618,7 @@ int wdit_fold_weight_batch(const wdit_fold_job* jobs, int n_jobs, void* stream) 
 
 int wdit_layernorm_modulation(const void* x, int x_is_bf16, int ldx, int M, int D, const float* scale,
                               const float* shift, float eps, void* out, int ldo, void* stream) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (x == nullptr || scale == nullptr || shift == nullptr || out == nullptr) return WDIT_ERR_ARG;
   if (M <= 0 || D <= 0 || D % 8 != 0 || ldx < D || ldo < D) return WDIT_ERR_SHAPE;
   if (!a16(x) || !a16(out) || ldx % 8 != 0 || ldo % 8 != 0) return WDIT_ERR_ALIGN;
@@ -622,6 +628,7 @@ int wdit_layernorm_modulation(const void* x, int x_is_bf16, int ldx, int M, int 
 }
 
 int wdit_rmsnorm(const void* x, int ldx, int M, int D, const float* w, float eps, void* out, int ldo, void* stream) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (x == nullptr || w == nullptr || out == nullptr) return WDIT_ERR_ARG;
   if (M <= 0 || D <= 0 || D % 8 != 0 || ldx < D || ldo < D) return WDIT_ERR_SHAPE;
   if (!a16(x) || !a16(out) || ldx % 8 != 0 || ldo % 8 != 0) return WDIT_ERR_ALIGN;
@@ -633,6 +640,7 @@ int wdit_rmsnorm(const void* x, int ldx, int M, int D, const float* w, float eps
 int wdit_qk_rms_rope_from_partials(void* qk, int ldqk, const float* partial, int M, int D, const float* wq,
                                    const float* wk, const float* cos_tab, const float* sin_tab, float eps,
                                    void* stream) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (qk == nullptr || partial == nullptr || wq == nullptr || wk == nullptr || cos_tab == nullptr ||
       sin_tab == nullptr)
     return WDIT_ERR_ARG;
@@ -656,6 +664,7 @@ int wdit_rope_table(const double* freqs_ri, int max_pos, int f, int h, int w, in
 
 int wdit_patch_rows(const void* latent, int C, int F, int H, int W, int pt, int ph, int pw, long long token_lo,
                     int rows, int Kp, void* out, void* stream) {
+  if (rows == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (latent == nullptr || out == nullptr) return WDIT_ERR_ARG;
   if (C <= 0 || pt <= 0 || ph <= 0 || pw <= 0 || F < pt || H < ph || W < pw || rows <= 0 || token_lo < 0)
     return WDIT_ERR_SHAPE;

@@ -983,6 +983,7 @@ int wdit_gemm_act(const void* A, int lda, const void* B, int ldb, void* out, int
                   const float* vec, int act, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
                   int ln_stats_width, float ln_eps, float* ms_out, int ms_ld, int ms_cols, void* stream,
                   int max_ctas) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   int rc = check_common(A, lda, B, ldb, M, N, K);
   if (rc) return rc;
   if (out == nullptr || ldo < N) return WDIT_ERR_ARG;
@@ -1017,6 +1018,7 @@ int wdit_gemm_residual(const void* A, int lda, const void* B, int ldb, const flo
                        int M, int N, int K, const float* bias, const float* gate_a, const float* gate_b,
                        int gate_b_stride, int rows_per_batch, void* x_bf16_out, int ldx, float* stats_out,
                        void* stream, int max_ctas) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   int rc = check_common(A, lda, B, ldb, M, N, K);
   if (rc) return rc;
   if (C == nullptr || out == nullptr || ldc < N || ldo < N) return WDIT_ERR_ARG;
@@ -1082,6 +1084,7 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
                    const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos, const float* rope_sin,
                    int rope_ld, int rows_per_batch, int token_offset, void* workspace, long long workspace_bytes,
                    void* stream, int max_ctas) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   int rc = check_norm(A, lda, B, ldb, out, ldo, M, N, K, vec, norm_groups, norm_width, norm_w0, norm_w1, rope_groups,
                       rope_cos, rope_sin, rope_ld, rows_per_batch, token_offset);
   if (rc) return rc;
@@ -1157,6 +1160,7 @@ int wdit_gemm_norm_static(const void* A, int lda, const void* B, int ldb, void* 
                           const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
                           const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream,
                           int max_ctas) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
   if (norm_groups < 1) return WDIT_ERR_ARG;
   int rc = check_norm(A, lda, B, ldb, out, ldo, M, N, K, vec, norm_groups, norm_width, norm_w0, norm_w1, rope_groups,
                       rope_cos, rope_sin, rope_ld, rows_per_batch, token_offset);

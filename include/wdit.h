@@ -15,6 +15,8 @@
  *     wait that ran out) are recorded on the device and read with wdit_read_error.
  *   - Alignment: every pointer 16-byte aligned; leading dimensions a multiple of 16 bytes.
  *   - N must be a multiple of 64 and K a multiple of 8 for the GEMMs; M is arbitrary.
+ *   - Zero rows (M = 0, or rows / N = 0 where those count the rows) is a no-op that returns
+ *     WDIT_OK before any pointer is looked at (an empty tensor may have a null data pointer).
  *
  * Each entry point names the reference (Owen718/CODA-Wan-DiT) interface it replaces.
  */

@@ -115,7 +115,7 @@ def test_patch_rows_validates_without_device(lib):
     dummy = ctypes.c_void_p(0x1000)
     assert lib.wdit_patch_rows(null, 16, 21, 60, 104, 1, 2, 2, 0, 32760, 64, dummy, null) == 1
     assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 32760, 56, dummy, null) == 2  # Kp < K
-    assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 0, 64, dummy, null) == 2      # no rows
+    assert lib.wdit_patch_rows(null, 16, 21, 60, 104, 1, 2, 2, 0, 0, 64, null, null) == 0        # no rows
     assert lib.wdit_patch_rows(dummy, 16, 21, 60, 104, 1, 2, 2, 0, 32760, 64, ctypes.c_void_p(0x1008), null) == 3
 
 
@@ -168,3 +168,24 @@ def test_binding_signatures_match_the_header(pkg):
                 assert a is ctypes.c_void_p or issubclass(a, ctypes._Pointer), f"{name} arg {i}: {p}"
             else:
                 assert a is want, f"{name} arg {i}: {p} vs {a}"
+
+
+def test_zero_rows_is_a_no_op_without_device(lib, pkg):
+    """M = 0 returns OK before any pointer is looked at (null pointers, no device)."""
+    null = ctypes.c_void_p(None)
+    assert lib.wdit_gemm_act(null, 64, null, 64, null, 64, 0, 64, 64, null, 0, null, null, 0, 0, 0.0, null, 0, 0,
+                             null, 0) == 0
+    assert lib.wdit_gemm_residual(null, 64, null, 64, null, 64, null, 64, 0, 64, 64, null, null, null, 0, 0, null, 0,
+                                  null, null, 0) == 0
+    assert lib.wdit_gemm_norm(null, 64, null, 64, null, 256, 0, 256, 64, null, null, null, 0, 0, 0.0, 1, 128, null,
+                              null, 1e-6, 0, null, null, 0, 0, 0, null, 0, null, 0) == 0
+    assert lib.wdit_gemm_norm_static(null, 64, null, 64, null, 256, 0, 256, 64, null, null, null, 0, 0, 0.0, 1, 128,
+                                     null, null, 1e-6, 0, null, null, 0, 0, 0, null, 0) == 0
+    assert lib.wdit_ln_stats(null, 1, 1536, 0, 1536, null, null, null, null) == 0
+    assert lib.wdit_layernorm_modulation(null, 1, 1536, 0, 1536, null, null, 1e-6, null, 1536, null) == 0
+    assert lib.wdit_rmsnorm(null, 1536, 0, 1536, null, 1e-6, null, 1536, null) == 0
+    assert lib.wdit_qk_rms_rope_from_partials(null, 3072, null, 0, 1536, null, null, null, null, 1e-6, null) == 0
+    assert lib.wdit_rms_apply_layers(null, 9216, 0, null, 72, 1536, null, 1e-6, 3, 3072, 24, 1536, null) == 0
+    assert lib.wdit_fold_weight(null, 64, 0, 64, 1.0, null, null, null, null, null, null, 64, null, null, null) == 0
+    jobs = (pkg._lib.FoldJob * 3)()  # all empty: nothing launched
+    assert lib.wdit_fold_weight_batch(jobs, 3, null) == 0

@@ -96,6 +96,26 @@ def test_patch_embedding_as_gemm(pkg, patch, shape, lo, rows):
     assert torch.count_nonzero(pr[valid:]) == 0 and torch.count_nonzero(pr[:, K:]) == 0
 
 
+def test_zero_rows(pkg):
+    """Empty inputs (M = 0) give empty outputs, launch nothing and leave no device error."""
+    ops = pkg.ops
+    a = torch.empty((0, 1536), dtype=torch.bfloat16, device=DEV)
+    w = rand((256, 1536), 0.02, seed=900)
+    assert ops.gemm_act(a, w, act="gelu_tanh").shape == (0, 256)
+    c = torch.empty((0, 256), dtype=torch.float32, device=DEV)
+    assert ops.gemm_residual(a, w, c, out=c).shape == (0, 256)
+    wn = torch.ones(256, dtype=torch.float32, device=DEV)
+    assert ops.gemm_norm(a, w, norm_groups=1, norm_width=256, norm_w=(wn, None)).shape == (0, 256)
+    x = torch.empty((0, 1536), dtype=torch.float32, device=DEV)
+    assert ops.ln_stats(x).shape == (0, 6, 2)
+    v = torch.zeros(1536, dtype=torch.float32, device=DEV)
+    assert ops.layernorm_modulation_bf16(x, v, v, 1e-6).shape == (0, 1536)
+    assert ops.rmsnorm_fused(a, v + 1.0, 1e-6).shape == (0, 1536)
+    assert ops.fold_weight_batch([dict(w=torch.empty((0, 64), dtype=torch.bfloat16, device=DEV), mult_c=1.0)])[0][0].shape == (0, 64)
+    torch.cuda.synchronize()
+    assert pkg._lib.read_error(clear=True) == (0, 0, 0, 0)
+
+
 def test_cross_kv_layers(pkg):
     """All blocks' cross-attention K/V in one GEMM + one RMSNorm launch equals gemm_norm per block."""
     L, D, M = 3, 1536, 300

@@ -317,7 +317,7 @@ def fold_weight_batch(specs: list[dict]) -> list[tuple[torch.Tensor, torch.Tenso
         csum = torch.empty(N, dtype=torch.float32, device=w.device)
         vec = torch.empty(N, dtype=torch.float32, device=w.device)
         bias = _f32vec(sp.get("bias"))
-        keep.append(bias)
+        keep.append(bias)  # converted operands stay referenced until the launch is enqueued
         j.W, j.ldw, j.N, j.K, j.mult_c = ptr(w), w.stride(0), N, K, float(sp["mult_c"])
         j.mult_a, j.mult_b = ptr(sp.get("mult_a")), ptr(sp.get("mult_b"))
         j.shift_a, j.shift_b, j.bias = ptr(sp.get("shift_a")), ptr(sp.get("shift_b")), ptr(bias)

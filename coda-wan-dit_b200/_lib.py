@@ -89,7 +89,7 @@ class FoldJob(ctypes.Structure):
     ]
 
 
-FOLD_JOBS_PER_LAUNCH = 64
+FOLD_JOBS_PER_LAUNCH = 64  # jobs per fold_batch_kernel launch (kMaxFoldJobs in csrc/aux.cu)
 
 
 def library_path() -> Path:

@@ -189,3 +189,9 @@ def test_zero_rows_is_a_no_op_without_device(lib, pkg):
     assert lib.wdit_fold_weight(null, 64, 0, 64, 1.0, null, null, null, null, null, null, 64, null, null, null) == 0
     jobs = (pkg._lib.FoldJob * 3)()  # all empty: nothing launched
     assert lib.wdit_fold_weight_batch(jobs, 3, null) == 0
+
+
+def test_fold_jobs_per_launch_matches_kernel(pkg):
+    src = (ROOT / "coda-wan-dit_b200" / "csrc" / "aux.cu").read_text()
+    m = re.search(r"constexpr int kMaxFoldJobs = (\d+);", src)
+    assert m and int(m.group(1)) == pkg._lib.FOLD_JOBS_PER_LAUNCH

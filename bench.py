@@ -201,7 +201,7 @@ def run_reference(args) -> None:
         "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded randn inputs, random-init weights)",
         "config": {"workload": "cfg3: Wan2.1-1.3B 30-layer DiT forward, CFG batch 2, N=32760/sample",
-                   "model": "Wan2.1-1.3B (random init)", "layers": args.layers, "global_batch": BATCH,
+                   "weights": "random init", "layers": args.layers, "global_batch": BATCH,
                    "seq_len": seq_len(), "latent": list(LATENT), "context": list(TEXT), "t": T_STEP,
                    "parallelism": "host cores (bounded sample, FLOP-extrapolated)"},
         "cpu_baseline": base,
@@ -326,7 +326,7 @@ def run_ours(args) -> None:
             "dtype": "bf16",
             "data": "synthetic (seeded randn latents/contexts, random-init weights; no checkpoint)",
             "config": {"workload": "cfg3: Wan2.1-1.3B 30-layer DiT forward, CFG batch 2, N=32760/sample",
-                       "model": "Wan2.1-1.3B (random init)", "layers": args.layers, "global_batch": BATCH,
+                       "weights": "random init", "layers": args.layers, "global_batch": BATCH,
                        "seq_len": L, "latent": list(LATENT), "context": list(TEXT), "t": T_STEP,
                        "parallelism": (f"sp{world} (token-sharded, Ulysses all-to-all over {args.transport})"
                                        if world > 1 else "single GPU"),

@@ -24,8 +24,9 @@ Per block, on one stream (M = B * L rows):
     FFN2 GEMM            x += (h W2^T + b2) * (mod5 + e5)    -> x, bf16 copy, LN stats
 
 The LayerNorm statistics and the bf16 copy of the residual stream produced by each residual
-epilogue are handed to the next block through a ``Carry`` keyed on the residual tensor's
-storage and version, so only the first block runs the standalone statistics pass.
+epilogue are handed to the next block through a ``Carry`` keyed on the residual tensor object
+(weakly referenced) and its version counter, so only the first block runs the standalone
+statistics pass.
 
 Differences from the reference's block, all deliberate:
   * batch > 1 (CFG) and any grid are accepted; ``freqs`` is used (the reference asserts
@@ -36,55 +37,89 @@ Differences from the reference's block, all deliberate:
 """
 from __future__ import annotations
 
+import threading
+import weakref
+
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
 from . import ops
 
-_ONE_SYNC_CACHE: dict = {}
+_ONE_SYNC = threading.local()
+
+
+def _root(t: torch.Tensor) -> torch.Tensor:
+    """The tensor object that owns the storage of `t` (views point to it through ``_base``)."""
+    return t._base if t._base is not None else t
 
 
 def _host_values(t):
-    """Python ints of a small tensor, read once per distinct tensor object / version."""
+    """Python ints of a small tensor, read once per distinct tensor object and version.
+
+    The cache entry holds a weak reference to the tensor it was read from: a new tensor that
+    happens to get the same ``id`` and address after the old one was freed is a miss."""
     if t is None:
         return None
     if not torch.is_tensor(t):
         return [list(v) if isinstance(v, (list, tuple)) else int(v) for v in t]
-    key = (id(t), t.data_ptr(), t._version)
-    hit = _ONE_SYNC_CACHE.get(key)
-    if hit is None:
-        if len(_ONE_SYNC_CACHE) > 64:
-            _ONE_SYNC_CACHE.clear()
-        hit = t.tolist()
-        _ONE_SYNC_CACHE[key] = hit
-    return hit
+    cache = getattr(_ONE_SYNC, "cache", None)
+    if cache is None:
+        cache = _ONE_SYNC.cache = {}
+    hit = cache.get(id(t))
+    if hit is not None and hit[0]() is t and hit[1] == t._version:
+        return hit[2]
+    if len(cache) > 64:
+        cache.clear()
+    vals = t.tolist()
+    cache[id(t)] = (weakref.ref(t), t._version, vals)
+    return vals
 
 
 class Carry:
-    """bf16 copy + LayerNorm statistics of the residual stream, valid for one tensor state."""
+    """bf16 copy + LayerNorm statistics of the residual stream, valid for one tensor state.
+
+    The key is the residual tensor itself (a weak reference to the tensor object that owns
+    its storage, so any view of it matches) and its version counter. The residual epilogues
+    update the fp32 stream in place through the C ABI, which torch does not see, so the block
+    bumps the version itself after its last write (``torch.autograd.graph.increment_version``)
+    and records the bumped version. A freed tensor whose address is reused by a new tensor,
+    or a tensor changed in place by torch ops since, is a miss: its statistics are recomputed.
+    """
 
     def __init__(self):
-        self.key = None
+        self.ref = None
+        self.version = -1
+        self.shape = None
         self.xb = None
         self.stats = None
 
-    @staticmethod
-    def key_of(x: torch.Tensor):
-        return (x.data_ptr(), x._version, tuple(x.shape), x.dtype)
-
     def get(self, x: torch.Tensor):
-        if self.key is not None and self.key == self.key_of(x):
+        if self.ref is None or x.dtype != torch.float32:
+            return None
+        if self.ref() is _root(x) and self.version == x._version and self.shape == tuple(x.shape):
             return self.xb, self.stats
         return None
 
     def put(self, x: torch.Tensor, xb: torch.Tensor, stats: torch.Tensor) -> None:
-        self.key = self.key_of(x)
+        self.ref = weakref.ref(_root(x))
+        self.version = x._version
+        self.shape = tuple(x.shape)
         self.xb = xb
         self.stats = stats
 
 
-_DEFAULT_CARRY = Carry()
+_DEFAULT_CARRY = threading.local()
+
+
+def default_carry() -> Carry:
+    """Per-thread carry shared by standalone blocks (blocks installed one by one, as the
+    reference installs its CodaFullBlock, hand the statistics of their output to the next
+    block through it)."""
+    c = getattr(_DEFAULT_CARRY, "carry", None)
+    if c is None:
+        c = _DEFAULT_CARRY.carry = Carry()
+    return c
 
 
 def local_attention(q, k, v, k_lens=None):
@@ -119,7 +154,7 @@ class FusedWanBlock(nn.Module):
         self.ffn_dim = int(inner.ffn[0].weight.shape[0])
         self.eps = float(inner.eps)
         self.rms_eps = float(getattr(sa, "eps", inner.eps))
-        self.carry = carry if carry is not None else _DEFAULT_CARRY
+        self.carry = carry  # None: the per-thread default carry
         self.workspace = None  # None: the per-device shared workspace (launches are stream-ordered)
         self.seq_parallel = None  # set by the model for token-sharded runs
         self.kernel_timer = None  # list: (start event, end event, flops) of each FFN1 GEMM launch
@@ -193,6 +228,9 @@ class FusedWanBlock(nn.Module):
             self._rope["given"] = (rope_cos.float().contiguous(), rope_sin.float().contiguous())
 
     # ------------------------------------------------------------------
+    def _carry(self) -> Carry:
+        return self.carry if self.carry is not None else default_carry()
+
     def _rope_tables(self, grid, freqs):
         if "given" in self._rope:
             return self._rope["given"]
@@ -206,8 +244,8 @@ class FusedWanBlock(nn.Module):
     def _input_stats(self, x2: torch.Tensor):
         """bf16 copy, fp32 residual buffer and LN statistics of the block input rows."""
         M, D = x2.shape
-        hit = self.carry.get(x2)
-        if hit is not None and x2.dtype == torch.float32:
+        hit = self._carry().get(x2)
+        if hit is not None:
             xb, stats = hit
             return x2, xb, stats
         stats = torch.empty((M, ops.stats_tiles(D), 2), dtype=torch.float32, device=x2.device)
@@ -309,9 +347,10 @@ class FusedWanBlock(nn.Module):
                 workspace=self.workspace,
             )
         if fused_exchange:
-            y = sp.self_attention_p2p(qkv, part, self.w_nq, self.w_nk, self.rms_eps, cos, sin, B, L, H, hd)
+            y = sp.self_attention_p2p(qkv, part, self.w_nq, self.w_nk, self.rms_eps, cos, sin, B, L, H, hd,
+                                      key_lens=_host_values(seq_lens))
         elif sp is not None:
-            y = sp.self_attention(qkv, B, L, H, hd)
+            y = sp.self_attention(qkv, B, L, H, hd, key_lens=_host_values(seq_lens))
         else:
             q = qkv[:, :D].view(B, L, H, hd)
             k = qkv[:, D:2 * D].view(B, L, H, hd)
@@ -368,7 +407,10 @@ class FusedWanBlock(nn.Module):
             h, self.w_2, x32, out=x32, bias=self.b_2, gate_a=mod[5], gate_b=ev[:, 5 * D:], gate_b_stride=gate_stride,
             rows_per_batch=rows_per_batch, x_bf16_out=xb, stats_out=stats,
         )
-        self.carry.put(x32, xb, stats)
+        # The residual epilogues wrote x32 in place through the C ABI: move its version so that
+        # torch (and the carry key) see the change.
+        torch.autograd.graph.increment_version(x32)
+        self._carry().put(x32, xb, stats)
         return x32.view(B, L, D)
 
     # ------------------------------------------------------------------

@@ -1140,7 +1140,11 @@ int static_scratch_address(void** out) {
   if (g_static_scratch_addr[dev] == nullptr) {
     void* addr = nullptr;
     e = cudaGetSymbolAddress(&addr, g_norm_static_scratch);
-    if (e != cudaSuccess || addr == nullptr) return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // the lookup's error is not sticky: do not leave it for a later launch check
+      return WDIT_ERR_CUDA_BASE + static_cast<int>(e);
+    }
+    if (addr == nullptr) return WDIT_ERR_ARG;
     g_static_scratch_addr[dev] = addr;
   }
   *out = g_static_scratch_addr[dev];

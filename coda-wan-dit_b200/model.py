@@ -141,32 +141,41 @@ class WanParams(nn.Module):
 
 def init_random_(module: nn.Module, seed: int) -> nn.Module:
     """Seeded random init: weights ~N(0, 0.02), biases ~N(0, 0.01), modulation ~N(0,1)/sqrt(dim),
-    norm weights 1 and biases 0."""
-    g = torch.Generator().manual_seed(seed)
+    norm weights 1 and biases 0. Drawn in fp32 on the parameters' device, then cast to each
+    parameter's dtype."""
+    first = next(module.parameters(), None)
+    dev = first.device if first is not None else torch.device("cpu")
+    g = torch.Generator(device=dev).manual_seed(seed)
     with torch.no_grad():
         for name, p in module.named_parameters():
             leaf = name.rsplit(".", 1)[-1]
             if "modulation" in name:
-                p.copy_(torch.randn(p.shape, generator=g) / p.shape[-1] ** 0.5)
+                p.copy_(torch.randn(p.shape, generator=g, device=dev) / p.shape[-1] ** 0.5)
             elif "norm" in name:
                 p.fill_(1.0 if leaf == "weight" else 0.0)
             elif leaf == "weight":
-                p.copy_(0.02 * torch.randn(p.shape, generator=g))
+                p.copy_(0.02 * torch.randn(p.shape, generator=g, device=dev))
             else:
-                p.copy_(0.01 * torch.randn(p.shape, generator=g))
+                p.copy_(0.01 * torch.randn(p.shape, generator=g, device=dev))
     return module
 
 
 def build_wan(s: WanShape = WAN_1_3B, seed: int = 0, device="cuda", num_layers: int | None = None) -> WanParams:
     """Random-init model with the stock layout, bf16 weights (time embedding / projection and
-    the modulation vectors fp32, as the stock model keeps them)."""
-    m = init_random_(WanParams(s, num_layers), seed)
-    m = m.to(device=device, dtype=torch.bfloat16)
-    m.time_embedding.float()
-    m.time_projection.float()
-    for blk in m.blocks:
-        blk.modulation.data = blk.modulation.data.float()
-    m.head.modulation.data = m.head.modulation.data.float()
+    the modulation vectors fp32, as the stock model keeps them). Built without a CPU copy of
+    the weights (the 14B shape is 28 GB in bf16): the parameters are allocated on `device` and
+    initialised there."""
+    with torch.device("meta"):
+        m = WanParams(s, num_layers)
+        m.freqs = None  # complex buffer: set on the device below, not cast to bf16
+        m = m.to(dtype=torch.bfloat16)
+        m.time_embedding.float()
+        m.time_projection.float()
+        for blk in m.blocks:
+            blk.modulation.data = blk.modulation.data.float()
+        m.head.modulation.data = m.head.modulation.data.float()
+    m = m.to_empty(device=device)
+    init_random_(m, seed)
     m.freqs = rope_freqs(1024, s.head_dim).to(device)
     return m
 
@@ -369,12 +378,10 @@ class FusedWanModel(nn.Module):
         context = self.embed_text(context_list, text_len)
         self.cross_kv(context)
         Lx = x.shape[1]
-        seq_lens = torch.tensor(lens, dtype=torch.long) if sp is None else None
+        # Per-sample token counts (global, also under token sharding, where the gathered-head
+        # attention masks each unit's keys past its sample's count); None when no sample is padded.
         grid_sizes = torch.tensor(grids, dtype=torch.long)
-        if any(n != seq_len for n in lens):
-            seq_lens_arg = seq_lens
-        else:
-            seq_lens_arg = None
+        seq_lens_arg = torch.tensor(lens, dtype=torch.long) if any(n != seq_len for n in lens) else None
         x = x.contiguous()
         for blk in self.model.blocks:
             x = blk(x, e0, seq_lens_arg, grid_sizes, self.freqs, context, None)

@@ -123,6 +123,22 @@ class SeqParallel:
         self._x: _Exchange | None = None
         self.epoch = 0
 
+    def unit_key_mask(self, key_lens, B: int, H: int, L: int, device) -> torch.Tensor | None:
+        """Key mask of this rank's (batch, head) units for padded samples: [1, U, 1, L] bool,
+        True where key token < the unit's sample length (global lengths, one per batch entry),
+        or None when no sample is shorter than L. Unit u = b * H + h lives on rank u // U, so
+        this rank's unit j belongs to batch entry (rank * U + j) // H."""
+        if key_lens is None:
+            return None
+        lens = [int(v) for v in key_lens]
+        if len(lens) != B:
+            raise ValueError(f"{len(lens)} sequence lengths for a batch of {B}")
+        if all(n >= L for n in lens):
+            return None
+        U = B * H // self.world
+        unit_len = torch.tensor([lens[(self.rank * U + j) // H] for j in range(U)], device=device)
+        return (torch.arange(L, device=device).view(1, 1, 1, L) < unit_len.view(1, U, 1, 1))
+
     @property
     def fuses_qk_norm(self) -> bool:
         """True when self_attention_p2p takes the raw QKV GEMM output and its RMSNorm partials."""
@@ -138,9 +154,10 @@ class SeqParallel:
 
     def self_attention_p2p(self, qkv: torch.Tensor, part: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
                            eps: float, cos: torch.Tensor, sin: torch.Tensor, B: int, Lp: int, H: int,
-                           hd: int) -> torch.Tensor:
+                           hd: int, key_lens=None) -> torch.Tensor:
         """qkv [B*Lp, 3*H*hd] raw QKV GEMM output of this rank's tokens, part [B*Lp, 2*H] its q/k
-        mean-square partials -> attention output [B*Lp, H*hd] for the same tokens."""
+        mean-square partials -> attention output [B*Lp, H*hd] for the same tokens. key_lens:
+        per-sample token counts (keys at or past a sample's count are masked), or None."""
         P = self.world
         assert Lp == self.local_len and (B * H) % P == 0 and hd == 128
         assert qkv.stride(1) == 1 and part.stride(1) == 1 and cos.stride(1) == 1 and sin.stride() == cos.stride()
@@ -158,7 +175,9 @@ class SeqParallel:
              x.full_off[buf], x.flag_off[0], e, ptr(x.done), st)
         call("wdit_p2p_wait", x.flags(0), P, e, st)
         full = x.full(buf, U, L, hd)
-        o = F.scaled_dot_product_attention(full[0].unsqueeze(0), full[1].unsqueeze(0), full[2].unsqueeze(0))[0]
+        mask = self.unit_key_mask(key_lens, B, H, L, qkv.device)
+        o = F.scaled_dot_product_attention(full[0].unsqueeze(0), full[1].unsqueeze(0), full[2].unsqueeze(0),
+                                           attn_mask=mask)[0]
         assert o.stride(2) == 1
         call("wdit_p2p_out_exchange", ptr(o), o.stride(0), o.stride(1), B, Lp, H, hd, P, self.rank, x.peers,
              x.y_off[buf], D, x.flag_off[1], e, ptr(x.done) + 4, st)
@@ -171,9 +190,10 @@ class SeqParallel:
         else:
             dist.all_to_all_single(out, inp, group=self.group)
 
-    def self_attention(self, qkv: torch.Tensor, B: int, Lp: int, H: int, hd: int) -> torch.Tensor:
+    def self_attention(self, qkv: torch.Tensor, B: int, Lp: int, H: int, hd: int, key_lens=None) -> torch.Tensor:
         """qkv [B*Lp, 3*H*hd] (rotated, normalized q/k and v of this rank's tokens) ->
-        attention output [B*Lp, H*hd] for the same tokens."""
+        attention output [B*Lp, H*hd] for the same tokens. key_lens: per-sample token counts
+        (keys at or past a sample's count are masked), or None."""
         P = self.world
         assert Lp == self.local_len and (B * H) % P == 0
         U = B * H // P
@@ -186,7 +206,9 @@ class SeqParallel:
         self._a2a(recv, send)
         full = torch.empty((3, U, L, hd), dtype=torch.bfloat16, device=dev)
         call("wdit_seq_gather", ptr(recv), 3, U, P, Lp, hd, ptr(full), stream_ptr())
-        o = F.scaled_dot_product_attention(full[0].unsqueeze(0), full[1].unsqueeze(0), full[2].unsqueeze(0))
+        mask = self.unit_key_mask(key_lens, B, H, L, dev)
+        o = F.scaled_dot_product_attention(full[0].unsqueeze(0), full[1].unsqueeze(0), full[2].unsqueeze(0),
+                                           attn_mask=mask)
         o = o[0]  # [U, L, hd], strides as returned by the attention backend
         assert o.stride(2) == 1
         send2 = torch.empty(P * U * Lp * hd, dtype=torch.bfloat16, device=dev)

@@ -1,6 +1,6 @@
 """Config 2: isolated fused-GEMM microbenchmark on one B200 (plus the memory-bound passes).
 
-    python coda-wan-dit_b200/microbench.py [--m 32760] [--only ffn1,ffn2,...] [--iters 20]
+    python microbench.py [--m 32760] [--only ffn1,ffn2,...] [--iters 20]
 
 Each kernel is timed alone with CUDA events (median of --iters launches after warm-up; the
 operands exceed the 126 MB L2 at the default M, so launches do not hit in L2 from the
@@ -28,7 +28,7 @@ from pathlib import Path
 
 import torch
 
-ROOT = Path(__file__).resolve().parent.parent
+ROOT = Path(__file__).resolve().parent
 
 
 def _pkg():

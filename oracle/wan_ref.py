@@ -333,23 +333,42 @@ class WanModelRef(nn.Module):
 # ---------------------------------------------------------------------------
 def init_weights_(module: nn.Module, seed: int, norm_jitter: float = 0.0) -> nn.Module:
     """Linear / conv weights ~N(0, 0.02), biases ~N(0, 0.01), modulation ~N(0,1)/sqrt(dim);
-    norm weights 1 (norm_jitter > 0 perturbs them, and norm3's bias, to exercise the folds)."""
-    g = torch.Generator().manual_seed(seed)
+    norm weights 1 (norm_jitter > 0 perturbs them, and norm3's bias, to exercise the folds).
+    The generator lives on the parameters' device (a module built on a GPU is initialised there;
+    its values then differ from a CPU-initialised one with the same seed)."""
+    first = next(module.parameters(), None)
+    dev = first.device if first is not None else torch.device("cpu")
+    g = torch.Generator(device=dev).manual_seed(seed)
+
+    def randn(shape):
+        return torch.randn(shape, generator=g, device=dev)
+
     with torch.no_grad():
         for name, p in module.named_parameters():
             leaf = name.rsplit(".", 1)[-1]
             if "modulation" in name:
-                p.copy_(torch.randn(p.shape, generator=g) / p.shape[-1] ** 0.5)
+                p.copy_(randn(p.shape) / p.shape[-1] ** 0.5)
             elif "norm" in name:
                 if leaf == "weight":
-                    p.copy_(1.0 + norm_jitter * torch.randn(p.shape, generator=g))
+                    p.copy_(1.0 + norm_jitter * randn(p.shape))
                 else:
-                    p.copy_(norm_jitter * torch.randn(p.shape, generator=g))
+                    p.copy_(norm_jitter * randn(p.shape))
             elif leaf == "weight":
-                p.copy_(0.02 * torch.randn(p.shape, generator=g))
+                p.copy_(0.02 * randn(p.shape))
             elif leaf == "bias":
-                p.copy_(0.01 * torch.randn(p.shape, generator=g))
+                p.copy_(0.01 * randn(p.shape))
     return module
+
+
+def model_on_device(cfg: WanConfig, compute_dtype: torch.dtype, device, seed: int,
+                    num_layers: int | None = None) -> "WanModelRef":
+    """A WanModelRef built directly on `device` (no CPU copy of the weights) and initialised
+    there with init_weights_ (fp32 parameters, the rotary frequencies in complex128)."""
+    with torch.device("meta"):
+        m = WanModelRef(cfg, compute_dtype, num_layers=num_layers)
+    m = m.to_empty(device=device)
+    m.freqs = rope_freqs(1024, cfg.head_dim).to(device)
+    return init_weights_(m, seed)
 
 
 def block_inputs(cfg: WanConfig, grid: tuple[int, int, int], batch: int, seed: int, ctx_len: int = 512,
@@ -383,3 +402,20 @@ def model_inputs(cfg: WanConfig, latent_fhw: tuple[int, int, int], batch: int, s
     ctx = [torch.randn(cfg.text_len, cfg.text_dim, generator=g).to(device) for _ in range(batch)]
     seq_len = f * (h // cfg.patch[1]) * (w // cfg.patch[2])
     return {"x": xs, "t": torch.full((batch,), float(t)), "context": ctx, "seq_len": seq_len}
+
+
+def stock_bf16_model(cfg: WanConfig, state: dict, device, num_layers: int | None = None) -> "WanModelRef":
+    """The stock forward in bf16 mixed precision with the weights of `state`: Linear and
+    attention in bf16; time embedding, time projection and the modulation vectors fp32 (the
+    reference's "eager" baseline, coda_wan/run_wan_coda.py:248-252)."""
+    m = model_on_device(cfg, torch.bfloat16, device, seed=0, num_layers=num_layers)
+    m.load_state_dict(state, strict=True)
+    freqs, m.freqs = m.freqs, None
+    m = m.to(torch.bfloat16)
+    m.freqs = freqs
+    m.time_embedding.float()
+    m.time_projection.float()
+    for b in m.blocks:
+        b.modulation.data = b.modulation.data.float()
+    m.head.modulation.data = m.head.modulation.data.float()
+    return m.eval()

@@ -156,3 +156,44 @@ def test_block_14b_shape(pkg):
     want = run(ref, inp, freqs)
     got = run(fused, inp, freqs, e=inp["e"][:1], ctx_dtype=torch.bfloat16)
     assert rel_l2(got, want) <= 1e-2 and max_abs(got, want) <= 5e-2
+
+
+def test_recycled_residual_address_is_not_a_stale_carry_hit(pkg):
+    """A standalone block's fp32 output carries its LayerNorm statistics to the next call. A
+    new fp32 tensor that the caching allocator places at the freed output's address (same
+    shape, version 0, different values) must not pick them up: every call recomputes from its
+    own x, as the reference's block does (coda_wan/run_wan_coda.py:166-173)."""
+    ref, _, fused = make_pair(pkg, seed=23)
+    inp = wan_ref.block_inputs(wan_ref.WAN_1_3B, (1, 20, 26), 1, seed=15, device=DEV)
+    freqs = wan_ref.rope_freqs(1024, 128).to(DEV)
+    x1 = inp["x"].clone()
+    out1 = run(fused, inp, freqs, x=x1, ctx_dtype=torch.bfloat16)  # fp32 x: updated in place
+    addr, shape = out1.data_ptr(), out1.shape
+    torch.cuda.synchronize()
+    del out1, x1
+    other = wan_ref.block_inputs(wan_ref.WAN_1_3B, (1, 20, 26), 1, seed=16)["x"]  # CPU, new values
+    x2 = other.to(DEV)  # a fresh tensor: version 0, like the freed one
+    assert x2.data_ptr() == addr and x2.shape == shape, "the allocator did not reuse the freed address"
+    assert x2._version == 0
+    want = run(ref, inp, freqs, x=other.to(DEV))
+    got = run(fused, inp, freqs, x=x2, ctx_dtype=torch.bfloat16)
+    assert rel_l2(got, want) <= 1e-2 and max_abs(got, want) <= 5e-2
+
+
+def test_in_place_change_between_blocks_is_seen(pkg):
+    """The block bumps the version counter of the fp32 stream it updates through the C ABI, so
+    a torch in-place op on the output before the next block invalidates the carried statistics."""
+    ref1, _, f1 = make_pair(pkg, seed=24)
+    ref2, _, f2 = make_pair(pkg, seed=25)
+    inp = wan_ref.block_inputs(wan_ref.WAN_1_3B, (1, 12, 20), 1, seed=17, device=DEV)
+    freqs = wan_ref.rope_freqs(1024, 128).to(DEV)
+    x = inp["x"].clone()
+    v0 = x._version
+    g = run(f1, inp, freqs, x=x, ctx_dtype=torch.bfloat16)
+    assert x._version > v0  # the in-place C-ABI update is visible to torch
+    w = run(ref1, inp, freqs)
+    g.mul_(0.5).add_(1.0)
+    w = w * 0.5 + 1.0
+    g = run(f2, inp, freqs, x=g, ctx_dtype=torch.bfloat16)
+    w = run(ref2, inp, freqs, x=w)
+    assert rel_l2(g, w) <= 1e-2 and max_abs(g, w) <= 5e-2

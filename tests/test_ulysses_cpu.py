@@ -87,3 +87,68 @@ def test_p2p_exchange_layout(pkg, B, Lp, H, P):
     spans = sorted(parts)
     for (o1, n1), (o2, _) in zip(spans, spans[1:]):
         assert o1 + n1 <= o2
+
+
+def _padded_worker(rank, world, port, B, L, H, hd, lens, q, k, v, ret):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from __graft_entry__ import load_package
+
+        sp = load_package().SeqParallel(None, world, rank, (1, 1, L), L, transport="nccl")
+        Lp = L // world
+        D = H * hd
+        rows = torch.cat([t[:, rank * Lp:(rank + 1) * Lp].reshape(B * Lp, D) for t in (q, k, v)], dim=1)
+        U = B * H // world
+        send = ulysses_ref.pack(rows, B, Lp, H, hd, 3, world)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send)
+        full = ulysses_ref.seq_gather(recv, 3, U, world, Lp, hd)
+        mask = sp.unit_key_mask(lens, B, H, L, "cpu")
+        o = F.scaled_dot_product_attention(full[0][None], full[1][None], full[2][None], attn_mask=mask)[0]
+        send2 = ulysses_ref.seq_scatter(o, U, world, Lp, hd)
+        recv2 = torch.empty_like(send2)
+        dist.all_to_all_single(recv2, send2)
+        ret[rank] = ulysses_ref.unpack(recv2, B, Lp, H, hd, world)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,B,H,lens", [(2, 2, 12, [16, 11]), (4, 2, 12, [5, 32])])
+def test_regroup_masks_padded_keys(world, B, H, lens):
+    """Token-sharded attention with a sample shorter than the padded length: each rank masks its
+    units' keys past their sample's length (SeqParallel.unit_key_mask), which equals the
+    single-GPU path's per-sample key mask."""
+    torch.manual_seed(1)
+    L, hd = 8 * world, 16
+    q, k, v = (torch.randn(B, L, H * hd) for _ in range(3))
+    mgr = mp.Manager()
+    ret = mgr.dict()
+    mp.start_processes(_padded_worker, args=(world, _free_port(), B, L, H, hd, lens, q, k, v, ret), nprocs=world,
+                       start_method="spawn", join=True)
+    Lp = L // world
+    kl = torch.tensor(lens).view(B, 1, 1, 1)
+    mask = torch.arange(L).view(1, 1, 1, L) < kl
+    ref = F.scaled_dot_product_attention(
+        q.view(B, L, H, hd).transpose(1, 2), k.view(B, L, H, hd).transpose(1, 2), v.view(B, L, H, hd).transpose(1, 2),
+        attn_mask=mask).transpose(1, 2).reshape(B, L, H * hd)
+    unmasked = F.scaled_dot_product_attention(
+        q.view(B, L, H, hd).transpose(1, 2), k.view(B, L, H, hd).transpose(1, 2),
+        v.view(B, L, H, hd).transpose(1, 2)).transpose(1, 2).reshape(B, L, H * hd)
+    assert not torch.allclose(ref, unmasked, atol=1e-3)  # the padding matters for this case
+    for r in range(world):
+        want = ref[:, r * Lp:(r + 1) * Lp].reshape(B * Lp, H * hd)
+        assert torch.allclose(ret[r], want, atol=1e-5, rtol=1e-5)
+
+
+def test_unit_key_mask_none_without_padding(pkg):
+    sp = pkg.SeqParallel(None, 8, 3, (1, 1, 64), 64, transport="nccl")
+    assert sp.unit_key_mask(None, 2, 12, 64, "cpu") is None
+    assert sp.unit_key_mask([64, 64], 2, 12, 64, "cpu") is None
+    m = sp.unit_key_mask([64, 40], 2, 12, 64, "cpu")
+    # rank 3 of 8 holds units 9, 10, 11 (batch 0, heads 9-11): nothing masked
+    assert m.shape == (1, 3, 1, 64) and bool(m.all())
+    m = pkg.SeqParallel(None, 8, 5, (1, 1, 64), 64, transport="nccl").unit_key_mask([64, 40], 2, 12, 64, "cpu")
+    # rank 5 holds units 15, 16, 17 (batch 1): keys 40.. masked
+    assert bool(m[..., :40].all()) and not bool(m[..., 40:].any())

@@ -377,8 +377,10 @@ class FusedWanBlock(nn.Module):
             ctx = context.reshape(Bc * Lc, D)
             if ctx.dtype != torch.bfloat16:
                 ctx = ctx.to(torch.bfloat16)
+            # split path: the same arithmetic as the model's all-blocks cross-K/V launch
             ckv = ops.gemm_norm(ctx, self.w_ckv, vec=self.b_ckv, norm_groups=1, norm_width=D,
-                                norm_w=(self.w_cnk, None), norm_eps=self.rms_eps, workspace=self.workspace)
+                                norm_w=(self.w_cnk, None), norm_eps=self.rms_eps, workspace=self.workspace,
+                                fused=False)
         ck = ckv[:, :D].view(Bc, Lc, H, hd)
         cv = ckv[:, D:].view(Bc, Lc, H, hd)
         cy = local_attention(cq.view(B, L, H, hd), ck, cv, context_lens).reshape(M, D)

@@ -25,6 +25,12 @@
 //                      cross-KV, text MLP, head; optionally the per-row mean square of the
 //                      bf16 output over each 128-column block (RMSNorm partials, consumed by
 //                      the in-place RMSNorm / RoPE pass in aux.cu).
+//   kEpiNorm           kEpiAct (identity activation) with the full-width WanRMSNorm (+ 3D RoPE)
+//                      of the leading column groups applied in the epilogue: QKV, cross-Q.
+//                      One CTA (pair) owns whole (row block, group) units of width/256 tiles,
+//                      sums each row's squares over the unit, and after the unit's last tile
+//                      normalizes / rotates the unit's columns in place from L2 while the MMA
+//                      runs ahead on the next unit (see norm_unit_pass).
 //   kEpiResidual       out_f32 = C + (acc + bias) * gate    self-O (gate), cross-O (no gate),
 //   kEpiResidualLongK  (short / long K)                     FFN2 (gate)
 //                      and optionally a bf16 copy of out plus per-row (mean, M2) partials
@@ -66,7 +72,7 @@ constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 // of A and one 128-row half of B, and holds its 128 accumulator rows in its own TMEM.
 constexpr uint32_t kPairStageBytes = kTileABytes + kTileBBytes / 2;  // 32 KB
 constexpr int kTmemCols = 2 * BN;  // two accumulator buffers
-enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiResidualLongK = 3 };
+enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiResidualLongK = 3, kEpiNorm = 4 };
 
 template <int KIND>
 struct Cfg;
@@ -76,6 +82,15 @@ struct Cfg<kEpiAct> {
   static constexpr int kPairStages = 6;
   // 8 warps x 2 staging buffers (32 rows x 32 bf16, 64-byte swizzle)
   static constexpr uint32_t kEpiBytes = 8 * 2 * kWarpStgBytes;
+  static constexpr int kNumCBuf = 0;
+  static constexpr int kEpiArrivals = 2 * kEpiThreads;
+};
+template <>
+struct Cfg<kEpiNorm> {
+  static constexpr int kStages = 4;
+  static constexpr int kPairStages = 6;
+  // kEpiAct's staging + the two column halves' per-row sums of squares [2][128] fp32
+  static constexpr uint32_t kEpiBytes = 8 * 2 * kWarpStgBytes + 2 * BM * 4;
   static constexpr int kNumCBuf = 0;
   static constexpr int kEpiArrivals = 2 * kEpiThreads;
 };
@@ -118,7 +133,7 @@ constexpr uint32_t smem_bytes() {
          Cfg<KIND>::kEpiBytes + 256 /*barriers + tmem slot*/;
 }
 static_assert(smem_bytes<kEpiAct, true>() <= 232448 && smem_bytes<kEpiResidualLongK, true>() <= 232448 &&
-                  smem_bytes<kEpiResidual, false>() <= 232448,
+                  smem_bytes<kEpiResidual, false>() <= 232448 && smem_bytes<kEpiNorm, true>() <= 232448,
               "configuration exceeds the 227 KB shared-memory limit");
 
 // ---------------------------------------------------------------------------
@@ -164,6 +179,75 @@ __device__ __forceinline__ void ln_row_stats(const LnFold& ln, int row, float& m
   rstd = rsqrtf(m2 / static_cast<float>(ln.row_len) + ln.eps);
 }
 
+// In-place WanRMSNorm (+ RoPE) of one finished (row block, group) unit of the norm GEMM, run by
+// the eight epilogue warps after the unit's last tile: warp ew takes rows ew, ew + 8, ... of
+// the CTA's 128-row block; per row, lane l holds the 16-byte vectors at columns
+// 8 l + 256 u of the group, so its rotary pairs are the same four, (l % 16) * 4 .. + 3, in
+// every head (one float4 of cos and one of sin per row). The unit's bf16 GEMM output was
+// stored by TMA and is read back from L2 (ld.global.cg). Arithmetic of
+// coda_wan/wan_coda_kernels.py:233-352 (_qk_rms_rope_kernel) and :371-411 (_rmsnorm_kernel):
+// rstd = rsqrt(mean(y^2) + eps) over the group's full width (y = the bf16 GEMM output),
+// z = bf16(bf16(y rstd) w), then (z_e cos - z_o sin, z_e sin + z_o cos) in fp32, one rounding.
+constexpr int kPassVec = 6;  // 16-byte vectors per lane in flight (one 1536-column row)
+
+__device__ __forceinline__ void norm_unit_pass(const NormParams& np, const float* ss_x, int m_blk, int g, int M,
+                                               int rows_per_batch, int ew, int lane) {
+  const float* wg = g == 0 ? np.w0 : np.w1;
+  const bool rope = g < np.rope_groups;
+#pragma unroll 1
+  for (int rr = ew; rr < BM; rr += 8) {
+    const int row = m_blk * BM + rr;
+    if (row >= M) break;
+    const float rstd = rsqrtf((ss_x[rr] + ss_x[BM + rr]) * np.inv_width + np.eps);
+    float cc[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+    if (rope) {
+      const size_t tok = static_cast<size_t>(row % rows_per_batch + np.token_offset);
+      const float4 c4 = __ldg(reinterpret_cast<const float4*>(np.cos + tok * np.rope_ld) + (lane & 15));
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(np.sin + tok * np.rope_ld) + (lane & 15));
+      cc[0] = c4.x; cc[1] = c4.y; cc[2] = c4.z; cc[3] = c4.w;
+      sn[0] = s4.x; sn[1] = s4.y; sn[2] = s4.z; sn[3] = s4.w;
+    }
+    __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(np.out) + static_cast<size_t>(row) * np.ldo +
+                          static_cast<size_t>(g) * np.width;
+#pragma unroll 1
+    for (int c0 = 0; c0 < np.width; c0 += 256 * kPassVec) {
+      uint4 raw[kPassVec];
+#pragma unroll
+      for (int u = 0; u < kPassVec; ++u) {
+        const int c = c0 + 256 * u + lane * 8;
+        if (c < np.width) raw[u] = ld_global_cg_v4(base + c);
+      }
+#pragma unroll
+      for (int u = 0; u < kPassVec; ++u) {
+        const int c = c0 + 256 * u + lane * 8;
+        if (c >= np.width) break;
+        const float4 wa = __ldg(reinterpret_cast<const float4*>(wg + c));
+        const float4 wb = __ldg(reinterpret_cast<const float4*>(wg + c + 4));
+        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t rw[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[2 * i] = __uint_as_float(rw[i] << 16);
+          v[2 * i + 1] = __uint_as_float(rw[i] & 0xFFFF0000u);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = bf16_round(bf16_round(v[i] * rstd) * wv[i]);
+        if (rope) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float e = v[2 * i], o = v[2 * i + 1];
+            v[2 * i] = e * cc[i] - o * sn[i];
+            v[2 * i + 1] = e * sn[i] + o * cc[i];
+          }
+        }
+        st_global_v4(base + c, pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                     pack_bf16x2(v[6], v[7]));
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
@@ -203,6 +287,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int mq = t / s.n_blocks;
     n_blk = t - mq * s.n_blocks;
     m_blk = PAIR ? 2 * mq + cta_rank : mq;
+  };
+  // This CTA's (pair's) tile sequence i = 0 .. my_count - 1 -> (m_blk, n_blk, upos).
+  // Plain kinds: tile t_first + i * t_step. kEpiNorm: first its units u = t_first + j * t_step
+  // (unit u = (row group u / norm_groups, group u % norm_groups), upos = tile index inside the
+  // unit), then a contiguous range of the plain tiles, sized so that every CTA (pair) ends up
+  // with at most ceil(all tiles / CTAs) tiles.
+  int my_count = 0;
+  int seq_units = 0, seq_vstart = 0;
+  if constexpr (KIND == kEpiNorm) {
+    const int G = t_step, c = t_first;
+    const int base = s.units / G, rem = s.units - (s.units / G) * G;
+    seq_units = base + (c < rem ? 1 : 0);
+    const int mg = s.units / s.norm_groups;
+    const int P = mg * s.plain_nblocks;
+    const int T = (s.units * s.unit_tiles + P + G - 1) / G;
+    const int v1 = max(0, T - s.unit_tiles * (base + 1));
+    const int v0 = max(0, T - s.unit_tiles * base);
+    int vs = min(c, rem) * v1 + max(0, c - rem) * v0;
+    int ve = vs + (c < rem ? v1 : v0);
+    vs = min(vs, P);
+    ve = min(ve, P);
+    seq_vstart = vs;
+    my_count = seq_units * s.unit_tiles + (ve - vs);
+  } else {
+    my_count = t_first < s.tiles ? (s.tiles - 1 - t_first) / t_step + 1 : 0;
+  }
+  auto coords = [&](int i, int& m_blk, int& n_blk, int& upos) {
+    if constexpr (KIND == kEpiNorm) {
+      int mq;
+      const int nu = seq_units * s.unit_tiles;
+      if (i < nu) {
+        const int j = i / s.unit_tiles;
+        upos = i - j * s.unit_tiles;
+        const int u = t_first + j * t_step;
+        mq = u / s.norm_groups;
+        n_blk = (u - mq * s.norm_groups) * s.unit_tiles + upos;
+      } else {
+        const int pidx = seq_vstart + (i - nu);
+        mq = pidx / s.plain_nblocks;
+        n_blk = s.norm_groups * s.unit_tiles + (pidx - mq * s.plain_nblocks);
+        upos = -1;
+      }
+      m_blk = PAIR ? 2 * mq + cta_rank : mq;
+    } else {
+      tile_coords(t_first + i * t_step, m_blk, n_blk);
+      upos = -1;
+    }
   };
 
   if (threadIdx.x == 0) {
@@ -245,9 +376,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = t_first; tile < s.tiles; tile += t_step) {
-        int m_blk, n_blk;
-        tile_coords(tile, m_blk, n_blk);
+      for (int i = 0; i < my_count; ++i) {
+        int m_blk, n_blk, upos;
+        coords(i, m_blk, n_blk, upos);
         for (int kb = 0; kb < s.k_blocks; ++kb) {
           if (!wait_parity<PAIR>(&empty_bar[stage], phase ^ 1u, kSiteProducerEmpty)) goto producer_done;
           uint8_t* st = stage_base + stage * SB;
@@ -287,8 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN);
       int stage = 0;
       uint32_t phase = 0;
-      int it = 0;
-      for (int tile = t_first; tile < s.tiles; tile += t_step, ++it) {
+      for (int it = 0; it < my_count; ++it) {
         const int buf = it & 1;
         const uint32_t tphase = (it >> 1) & 1;
         if (!wait_parity<PAIR>(&tempty_bar[buf], tphase ^ 1u, kSiteMmaTmemEmpty)) break;
@@ -358,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
 
-    if constexpr (KIND == kEpiAct) {
+    if constexpr (KIND == kEpiAct || KIND == kEpiNorm) {
       constexpr int kChunks = (BN / 2) / 32;  // 32-column chunks per half
       // Per-warp staging: two 32-row x 32-column bf16 buffers (64-byte swizzle) per warp, each
       // stored by the warp's own TMA store, so the warps of a half never wait on each other.
@@ -366,10 +496,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t stg_warp = smem_u32(stg_warp_ptr);
       const bool use_ln = p.ln.csum != nullptr;
       int sbuf = 0;
-      int it = 0;
-      for (int tile = t_first; tile < s.tiles; tile += t_step, ++it) {
-        int m_blk, n_blk;
-        tile_coords(tile, m_blk, n_blk);
+      // kEpiNorm: this thread's sum of squares of its row over the current unit's columns of
+      // its half, and the two halves' sums exchanged at the end of each unit.
+      uint64_t unit_ss2 = f2_pack(0.f, 0.f);
+      float* ss_x = reinterpret_cast<float*>(epi_base + 8 * 2 * kWarpStgBytes);
+      for (int it = 0; it < my_count; ++it) {
+        int m_blk, n_blk, upos;
+        coords(it, m_blk, n_blk, upos);
         const int warp_row0 = m_blk * BM + wq * 32;
         const bool rows_any = warp_row0 < s.M;  // this warp's 32 rows hold data
         const int buf = it & 1;
@@ -392,9 +525,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t tbase = tmem_base + lane_off + buf * BN + col_base;
-        // RMSNorm partials: this half's 128 columns form one partial block.
-        const bool ss_on = p.ss_part != nullptr && nh < p.ss_cols;
-        uint64_t ss2 = f2_pack(0.f, 0.f);
+        // RMSNorm partials: this half's 128 columns form one partial block (kEpiAct), or
+        // the running sum over the unit (kEpiNorm).
+        const bool ss_on = KIND == kEpiNorm ? upos >= 0 : (p.ss_part != nullptr && nh < p.ss_cols);
+        uint64_t ss2 = KIND == kEpiNorm ? unit_ss2 : f2_pack(0.f, 0.f);
 #pragma unroll 1
         for (int c = 0; c < kChunks; ++c) {
           const int n0 = nh + c * 32;
@@ -462,10 +596,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           sbuf ^= 1;
         }
-        if (ss_on && row_ok) {
-          float s0, s1;
-          f2_unpack(ss2, s0, s1);
-          p.ss_part[static_cast<size_t>(row) * p.ss_ld + (nh >> 7)] = (s0 + s1) * (1.f / 128.f);
+        if constexpr (KIND == kEpiNorm) {
+          unit_ss2 = ss2;
+          if (upos == s.unit_tiles - 1) {
+            // Unit done: merge the halves' sums, make this CTA's TMA stores of the unit visible
+            // to generic loads, and normalize / rotate the unit's columns in place.
+            float s0, s1;
+            f2_unpack(unit_ss2, s0, s1);
+            ss_x[half * BM + r] = s0 + s1;
+            unit_ss2 = f2_pack(0.f, 0.f);
+            if (lane == 0) {
+              bulk_wait_all<0>();
+              fence_proxy_async_global();
+            }
+            __syncwarp();
+            named_bar_sync(5, 2 * kEpiThreads);
+            norm_unit_pass(p.norm, ss_x, m_blk, n_blk / s.unit_tiles, s.M, p.rows_per_batch, ew, lane);
+          }
+        } else {
+          if (ss_on && row_ok) {
+            float s0, s1;
+            f2_unpack(ss2, s0, s1);
+            p.ss_part[static_cast<size_t>(row) * p.ss_ld + (nh >> 7)] = (s0 + s1) * (1.f / 128.f);
+          }
         }
       }
       if (lane == 0) bulk_wait_all<0>();
@@ -789,6 +942,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, con
   }
   GemmShape s = shape;
   int grid = num_sms();
+  if (s.norm_groups > 0) s.units = (PAIR ? (s.m_blocks + 1) / 2 : s.m_blocks) * s.norm_groups;
   if (PAIR) {
     s.tiles = ((s.m_blocks + 1) / 2) * s.n_blocks;  // 256-row pair tiles
     grid = 2 * pair_slots[dev & 63];
@@ -813,7 +967,7 @@ int check_common(const void* A, int lda, const void* B, int ldb, int M, int N, i
 }
 
 GemmShape make_shape(int M, int N, int K) {
-  GemmShape s;
+  GemmShape s = {};
   s.M = M;
   s.N = N;
   s.K = K;
@@ -915,6 +1069,46 @@ int run_norm(const void* A, int lda, const void* B, int ldb, void* out, int ldo,
   return launch_rms_rope_apply(out, ldo, M, part, p.ss_ld, norm_groups, norm_width, norm_w0, norm_w1, norm_eps,
                                rope_groups, rope_cos, rope_sin, rope_ld, rows_per_batch > 0 ? rows_per_batch : M,
                                token_offset, stream);
+}
+
+// The same result in one launch: the norm GEMM with the RMSNorm / RoPE in its epilogue.
+int run_norm_fused(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                   const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                   int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
+                   const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
+                   const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, cudaStream_t stream,
+                   int max_ctas) {
+  EpiParams p = {};
+  int rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
+  if (rc) return rc;
+  p.vec = vec;
+  p.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
+  p.has_out_map = 1;
+  NormParams& np = p.norm;
+  np.out = out;
+  np.ldo = ldo;
+  np.width = norm_width;
+  np.inv_width = 1.f / static_cast<float>(norm_width);
+  np.eps = norm_eps;
+  np.w0 = norm_w0;
+  np.w1 = norm_w1;
+  np.rope_groups = rope_groups;
+  np.cos = rope_cos;
+  np.sin = rope_sin;
+  np.rope_ld = rope_ld;
+  np.token_offset = token_offset;
+  const bool pair = use_pair(M);
+  CUtensorMap ma, mb, mo, none;
+  memset(&none, 0, sizeof(none));
+  if ((rc = build_ab(&ma, &mb, A, lda, B, ldb, M, N, K, pair))) return rc;
+  if ((rc = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, N, M, ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
+    return rc;
+  GemmShape shape = make_shape(M, N, K);
+  shape.norm_groups = norm_groups;
+  shape.unit_tiles = norm_width / BN;
+  shape.plain_nblocks = shape.n_blocks - norm_groups * shape.unit_tiles;
+  return pair ? launch<kEpiNorm, true>(ma, mb, mo, none, none, shape, p, stream, max_ctas)
+              : launch<kEpiNorm, false>(ma, mb, mo, none, none, shape, p, stream, max_ctas);
 }
 
 }  // namespace
@@ -1097,6 +1291,23 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
                   norm_groups, norm_width, norm_w0, norm_w1, norm_eps, rope_groups, rope_cos, rope_sin, rope_ld,
                   rows_per_batch, token_offset, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream),
                   max_ctas);
+}
+
+int wdit_gemm_norm_fused(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                         const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                         int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
+                         const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
+                         const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream,
+                         int max_ctas) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
+  if (norm_groups < 1) return WDIT_ERR_ARG;
+  int rc = check_norm(A, lda, B, ldb, out, ldo, M, N, K, vec, norm_groups, norm_width, norm_w0, norm_w1, rope_groups,
+                      rope_cos, rope_sin, rope_ld, rows_per_batch, token_offset);
+  if (rc) return rc;
+  if (norm_width % BN != 0) return WDIT_ERR_SHAPE;  // units are whole N tiles
+  return run_norm_fused(A, lda, B, ldb, out, ldo, M, N, K, vec, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width,
+                        ln_eps, norm_groups, norm_width, norm_w0, norm_w1, norm_eps, rope_groups, rope_cos, rope_sin,
+                        rope_ld, rows_per_batch, token_offset, static_cast<cudaStream_t>(stream), max_ctas);
 }
 
 }  // extern "C"

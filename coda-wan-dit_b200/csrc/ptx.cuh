@@ -125,6 +125,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's completed async-proxy (TMA) writes to global memory before its later
+// generic-proxy accesses (and, through a following barrier, other threads' accesses).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -407,6 +413,16 @@ __device__ __forceinline__ void ld_shared_v4(uint32_t addr, float& a, float& b, 
                : "=f"(a), "=f"(b), "=f"(c), "=f"(d)
                : "r"(addr)
                : "memory");
+}
+
+// 16-byte global load cached in L2 only (data another thread of the CTA just wrote).
+__device__ __forceinline__ uint4 ld_global_cg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
 }
 
 __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {

@@ -7,6 +7,26 @@ namespace wdit {
 struct GemmShape {
   int M, N, K;
   int m_blocks, n_blocks, k_blocks, tiles;
+  // Unit schedule of the norm GEMM (kEpiNorm; zero otherwise): the leading norm_groups column
+  // groups of `unit_tiles` N tiles each are processed one (row block, group) unit at a time by
+  // one CTA (pair); the remaining `plain_nblocks` N tiles of every row block are plain tiles.
+  int norm_groups, unit_tiles, plain_nblocks, units;
+};
+
+// Full-width RMSNorm (+ RoPE) applied by the norm GEMM's epilogue (kEpiNorm).
+struct NormParams {
+  void* out;            // bf16 output (the GEMM's), rows of ldo elements
+  int ldo;
+  int width;            // columns per normalized group (multiple of 256)
+  float inv_width;
+  float eps;
+  const float* w0;      // RMSNorm weight of group 0 [width]
+  const float* w1;      // ... of group 1 (norm_groups == 2)
+  int rope_groups;      // leading groups that also get the RoPE rotation
+  const float* cos;     // token-major [tokens, rope_ld] fp32 tables
+  const float* sin;
+  int rope_ld;
+  int token_offset;     // token of row m: m % rows_per_batch + token_offset
 };
 
 // adaLN LayerNorm absorbed into a GEMM:  rstd * (acc - mu * csum[n]).
@@ -38,6 +58,7 @@ struct EpiParams {
   int ldx;
   int has_out_map;
   int has_x_map;
+  NormParams norm;  // kEpiNorm only
 };
 
 // In-place full-width RMSNorm (+ RoPE) of the leading column groups of a bf16 matrix from

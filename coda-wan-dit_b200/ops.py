@@ -194,11 +194,16 @@ def _ws_for(device) -> Workspace:
 
 def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_width=0, norm_w=(None, None),
               norm_eps=1e-6, rope_groups=0, rope_cos=None, rope_sin=None, rows_per_batch=0, token_offset=0,
-              out=None, workspace: Workspace | None = None, max_ctas=0):
+              out=None, workspace: Workspace | None = None, max_ctas=0, fused: bool | None = None):
     """out[M,N] bf16 = RoPE(RMSNorm_fullwidth(bf16(LN(a @ w.T) + vec))) per column group.
 
     rope_cos / rope_sin are token-major [T, 64] fp32 tables (row = token, column = rotary pair;
     any row stride that is a multiple of 4), as build_wan_rope_table returns them.
+
+    fused: True = one launch with the RMSNorm / RoPE in the GEMM epilogue (wdit_gemm_norm_fused,
+    no workspace; norm_width a multiple of 256); False = the GEMM + partials, then the in-place
+    RMSNorm / RoPE pass (wdit_gemm_norm, the reference's two-kernel split); None = fused when
+    the width allows it.
     """
     _require_cuda(a, w)
     a = _rowmajor(a)
@@ -207,9 +212,11 @@ def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_w
     assert w.shape[1] == K and w.stride(1) == 1
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    if fused is None:
+        fused = norm_groups > 0 and norm_width % 256 == 0
     ws = None
     nbytes = 0
-    if norm_groups > 0:
+    if norm_groups > 0 and not fused:
         ws = (workspace or _ws_for(a.device)).get(M, N, norm_groups, norm_width, a.device)
         nbytes = ws.numel()
     w0 = _f32vec(norm_w[0]) if norm_groups > 0 else None
@@ -222,6 +229,15 @@ def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_w
         assert rope_cos.stride(1) == 1 and rope_sin.stride() == rope_cos.stride()
         assert rope_cos.shape[0] >= (rows_per_batch or M) + token_offset, "RoPE tables shorter than the tokens"
         rope_ld = rope_cos.stride(0)
+    if fused:
+        call(
+            "wdit_gemm_norm_fused",
+            ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(out), out.stride(0), M, N, K,
+            ptr(vec), *_ln_args(ln, K), norm_groups, norm_width, ptr(w0), ptr(w1), float(norm_eps),
+            rope_groups, ptr(rope_cos), ptr(rope_sin), rope_ld, rows_per_batch, token_offset,
+            stream_ptr(), max_ctas,
+        )
+        return out
     call(
         "wdit_gemm_norm",
         ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(out), out.stride(0), M, N, K,

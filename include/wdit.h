@@ -127,6 +127,26 @@ int wdit_gemm_norm(const void* A, int lda, const void* B, int ldb, void* out, in
                    void* stream, int max_ctas);
 
 /*
+ * The result of wdit_gemm_norm in ONE launch and without a workspace: the GEMM's epilogue
+ * applies the full-width RMSNorm and RoPE itself. Each CTA pair owns whole (row block, group)
+ * units of norm_width / 256 output tiles, sums each row's squares of the bf16 output over the
+ * unit, and after the unit's last tile normalizes / rotates the unit's columns in place (from
+ * L2) while its tensor cores start the next unit. Requires norm_groups >= 1 and
+ * norm_width % 256 == 0 (else WDIT_ERR_ARG / WDIT_ERR_SHAPE; wdit_gemm_norm takes any
+ * multiple of 128). Same arguments and arithmetic as wdit_gemm_norm otherwise; the mean square
+ * is summed in another order, so results can differ from wdit_gemm_norm's by a bf16 ulp.
+ * Replaces: coda_wan/wan_coda_kernels.py:355-368 qk_coda_rms_rope (the Q+K GEMM :192-230 and
+ * the RMSNorm / RoPE kernel :313-352 in one), the V projection at coda_wan/run_wan_coda.py:158,
+ * and :371-411 rmsnorm_fused applied to the cross-attention q (coda_wan/run_wan_coda.py:177-179).
+ */
+int wdit_gemm_norm_fused(const void* A, int lda, const void* B, int ldb, void* out, int ldo, int M, int N, int K,
+                         const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                         int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
+                         const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
+                         const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, void* stream,
+                         int max_ctas);
+
+/*
  * wdit_gemm_norm without a workspace argument: it allocates nothing and takes no scratch from
  * the caller. No counterpart in the reference (which always allocates through PyTorch); it is
  * for callers that cannot allocate device memory where they issue this GEMM, e.g. code running

@@ -11,9 +11,10 @@ torch.matmul (cuBLAS, bf16) time for context.
 Shapes (Wan2.1-1.3B, batch 1, N = 32760 tokens):
   ffn1   [M x 1536] . [1536 x 8960]  LayerNorm folded + shift term + bias + tanh-GELU -> bf16
   ffn2   [M x 8960] . [8960 x 1536]  (acc + b) * gate + residual -> fp32, + bf16 copy + LN stats
-  qkv    [M x 1536] . [1536 x 4608]  LN folded, full-width q/k RMSNorm, 3D RoPE -> bf16
+  qkv    [M x 1536] . [1536 x 4608]  LN folded, full-width q/k RMSNorm, 3D RoPE -> bf16 (one launch;
+                                     qkv_split: GEMM + partials, then the RMSNorm / RoPE pass)
   self_o [M x 1536] . [1536 x 1536]  gate + residual (+ bf16 copy + stats)
-  cross_q[M x 1536] . [1536 x 1536]  norm3 folded + RMSNorm
+  cross_q[M x 1536] . [1536 x 1536]  norm3 folded + RMSNorm (cross_q_split: two launches)
   cross_o[M x 1536] . [1536 x 1536]  bias + residual (+ bf16 copy + stats)
   stats  LayerNorm statistics pass over fp32 [M x 1536]   (reads 4 B, writes 8 B per row... HBM)
   fold   per-step weight fold of the FFN1 weight [8960 x 1536] (reads 2 B + writes 2 B / weight)
@@ -132,7 +133,9 @@ def run(M: int = 32760, only: set[str] | None = None, iters: int = 20, cublas: b
         ms = _time(lambda: ops.gemm_residual(h, w, c, out=c, bias=b, gate_a=gate, x_bf16_out=xo, stats_out=so),
                    iters)
         add("ffn2", ms, 2.0 * M * D * F, cublas_ms=cub(h, w))
-    if want("qkv"):
+    for name, fused in (("qkv", True), ("qkv_split", False)):
+        if not want(name):
+            continue
         w = rnd((3 * D, D), 0.02)
         s = rnd((D,), 0.1, torch.float32)
         wf, cs, vec = ops.fold_weight(w, mult_c=1.0, mult_a=s, shift_a=s)
@@ -144,8 +147,8 @@ def run(M: int = 32760, only: set[str] | None = None, iters: int = 20, cublas: b
         ws = ops.Workspace()
         ms = _time(lambda: ops.gemm_norm(xb, wf, vec=vec, ln=ln, norm_groups=2, norm_width=D, norm_w=(nw, nw),
                                          rope_groups=2, rope_cos=cos, rope_sin=sin, rows_per_batch=M, out=out,
-                                         workspace=ws), iters)
-        add("qkv", ms, 2.0 * M * 3 * D * D, cublas_ms=cub(xb, wf))
+                                         workspace=ws, fused=fused), iters)
+        add(name, ms, 2.0 * M * 3 * D * D, cublas_ms=cub(xb, wf))
     for name, gate in (("self_o", True), ("cross_o", False)):
         if want(name):
             a = rnd((M, D))
@@ -158,7 +161,9 @@ def run(M: int = 32760, only: set[str] | None = None, iters: int = 20, cublas: b
             ms = _time(lambda: ops.gemm_residual(a, w, c, out=c, bias=b, gate_a=gt, x_bf16_out=xo, stats_out=so),
                        iters)
             add(name, ms, 2.0 * M * D * D, cublas_ms=cub(a, w))
-    if want("cross_q"):
+    for name, fused in (("cross_q", True), ("cross_q_split", False)):
+        if not want(name):
+            continue
         w = rnd((D, D), 0.02)
         gm = 1.0 + rnd((D,), 0.1, torch.float32)
         wf, cs, vec = ops.fold_weight(w, mult_c=0.0, mult_a=gm, shift_a=gm)
@@ -167,8 +172,8 @@ def run(M: int = 32760, only: set[str] | None = None, iters: int = 20, cublas: b
         ln = ops.LnFold(cs, stats, 1e-6)
         ws = ops.Workspace()
         ms = _time(lambda: ops.gemm_norm(xb, wf, vec=vec, ln=ln, norm_groups=1, norm_width=D, norm_w=(nw, None),
-                                         out=out, workspace=ws), iters)
-        add("cross_q", ms, 2.0 * M * D * D, cublas_ms=cub(xb, wf))
+                                         out=out, workspace=ws, fused=fused), iters)
+        add(name, ms, 2.0 * M * D * D, cublas_ms=cub(xb, wf))
     pkg._lib.raise_on_device_error()
     return res
 

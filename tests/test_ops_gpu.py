@@ -127,7 +127,7 @@ def test_cross_kv_layers(pkg):
     assert got.shape == (M, 2 * D * L)
     for i in range(L):
         want = pkg.ops.gemm_norm(ctx, ws[i], vec=bs[i], norm_groups=1, norm_width=D, norm_w=(wks[i], None),
-                                 norm_eps=1e-6)
+                                 norm_eps=1e-6, fused=False)
         assert torch.equal(got[:, 2 * D * i:2 * D * (i + 1)], want)
 
 
@@ -238,8 +238,9 @@ def test_gemm_residual_per_batch_gate(pkg):
     assert rel_l2(got, c + acc * gate) < 1e-4
 
 
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("M", [1, 200, 300, 4095])
-def test_gemm_norm_qkv_rms_rope(pkg, M):
+def test_gemm_norm_qkv_rms_rope(pkg, M, fused):
     D, K = 1536, 1536
     a = rand((M, K), seed=30)
     w = rand((3 * D, K), 0.02, seed=31)
@@ -255,17 +256,19 @@ def test_gemm_norm_qkv_rms_rope(pkg, M):
     for rep in range(2):  # the second launch reuses the workspace left by the first
         got = pkg.ops.gemm_norm(a, w, vec=b, norm_groups=2, norm_width=D, norm_w=(wq, wk), norm_eps=1e-6,
                                 rope_groups=2, rope_cos=cos, rope_sin=sin, rows_per_batch=M, token_offset=17,
-                                workspace=ws)
+                                workspace=ws, fused=fused)
         assert rel_l2(got, want) < 5e-3, rep
 
 
-def test_gemm_norm_cross_kv_and_layernorm_fold(pkg):
+@pytest.mark.parametrize("fused", [True, False])
+def test_gemm_norm_cross_kv_and_layernorm_fold(pkg, fused):
     M, D = 512, 1536
     ctx = rand((M, D), seed=40)
     w = rand((2 * D, D), 0.02, seed=41)
     b = rand((2 * D,), 0.01, seed=42, dtype=torch.float32)
     wk = 1.0 + rand((D,), 0.1, seed=43, dtype=torch.float32)
-    got = pkg.ops.gemm_norm(ctx, w, vec=b, norm_groups=1, norm_width=D, norm_w=(wk, None), norm_eps=1e-6)
+    got = pkg.ops.gemm_norm(ctx, w, vec=b, norm_groups=1, norm_width=D, norm_w=(wk, None), norm_eps=1e-6,
+                            fused=fused)
     want = fused_ref.norm_epilogue(ctx.float() @ w.float().t() + b, 1, D, (wk,), 1e-6)
     assert rel_l2(got, want) < 5e-3
     # cross-Q: affine LayerNorm (norm3) folded statically, then RMSNorm
@@ -277,10 +280,56 @@ def test_gemm_norm_cross_kv_and_layernorm_fold(pkg):
     wf, cs, vec = pkg.ops.fold_weight(wq, mult_c=0.0, mult_a=gamma, shift_a=beta, bias=bq)
     stats = pkg.ops.ln_stats(x)
     got = pkg.ops.gemm_norm(x.to(torch.bfloat16), wf, vec=vec, ln=pkg.ops.LnFold(cs, stats, 1e-6), norm_groups=1,
-                            norm_width=D, norm_w=(wk, None), norm_eps=1e-6)
+                            norm_width=D, norm_w=(wk, None), norm_eps=1e-6, fused=fused)
     ln = torch.nn.functional.layer_norm(x, (D,), gamma, beta, 1e-6)
     want = fused_ref.norm_epilogue(ln.to(torch.bfloat16).float() @ wq.float().t() + bq, 1, D, (wk,), 1e-6)
     assert rel_l2(got, want) < 1e-2
+
+
+@pytest.mark.parametrize("M,D,groups,rope,rpb,N_extra", [
+    (65520, 1536, 2, 2, 32760, 1536),   # cfg3 QKV: CFG batch 2 (token = row % 32760), CTA pairs
+    (65520, 1536, 1, 0, 0, 0),          # cfg3 cross-Q
+    (256, 1536, 2, 2, 0, 1536),         # one 256-row block: single-CTA tiles
+    (4095, 1536, 2, 2, 0, 1536),        # ragged last row block (8 GPUs' shard)
+    (777, 5120, 2, 2, 0, 5120),         # 14B shape: 20-tile units, plain V tiles
+    (1000, 1536, 1, 0, 0, 1536),        # cross-KV: one normalized group, plain V after it
+    (300, 512, 2, 1, 0, 64),            # two 2-tile units, rope on q only, a partial plain tile
+])
+def test_gemm_norm_fused_equals_split(pkg, M, D, groups, rope, rpb, N_extra):
+    """The one-launch norm GEMM (RMSNorm / RoPE in the epilogue, unit schedule) against the
+    two-launch split path on the same inputs: the GEMM outputs are bit-identical, and the
+    normalized values differ at most by the mean square's summation order (one bf16 ulp)."""
+    K = 1536
+    N = groups * D + N_extra
+    a = rand((M, K), seed=60)
+    w = rand((N, K), 0.02, seed=61)
+    b = rand((N,), 0.01, seed=62, dtype=torch.float32)
+    wq = 1.0 + rand((D,), 0.1, seed=63, dtype=torch.float32)
+    wk = 1.0 + rand((D,), 0.1, seed=64, dtype=torch.float32)
+    tokens = (rpb or M) + 5
+    ang = rand((tokens, 64), 3.0, seed=65, dtype=torch.float32)
+    cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+    kw = dict(vec=b, norm_groups=groups, norm_width=D, norm_w=(wq, wk if groups > 1 else None), norm_eps=1e-6,
+              rope_groups=rope, rope_cos=cos if rope else None, rope_sin=sin if rope else None,
+              rows_per_batch=rpb, token_offset=5 if rope else 0)
+    split = pkg.ops.gemm_norm(a, w, fused=False, **kw)
+    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=DEV)
+    fused = pkg.ops.gemm_norm(a, w, fused=True, out=out, **kw)
+    torch.cuda.synchronize()
+    nc = groups * D
+    assert torch.equal(fused[:, nc:], split[:, nc:])  # plain columns: same GEMM, same rounding
+    f, s_ = fused[:, :nc].float(), split[:, :nc].float()
+    assert not torch.isnan(f).any()
+    # a last-bit change of rstd moves an element by at most about a bf16 ulp of the larger
+    # input of its rotation pair: bound by 2^-6 of the row's largest magnitude
+    row_scale = s_.abs().amax(dim=1, keepdim=True)
+    assert bool(((f - s_).abs() <= 2.0 ** -6 * row_scale).all())
+    assert (f == s_).float().mean().item() > 0.99
+    if M <= 4096:  # and against the oracle (per-row tables: token = row % rows_per_batch + 5)
+        tok = 5 + torch.arange(M, device=DEV) % (rpb or M)
+        acc = a.float() @ w.float().t() + b
+        want = fused_ref.norm_epilogue(acc, groups, D, (wq, wk)[:groups], 1e-6, rope, cos[tok], sin[tok])
+        assert rel_l2(fused, want) < 5e-3
 
 
 # --- reference op API against the golden fixtures (the reference's own outputs) ---

@@ -30,7 +30,7 @@
 //                      One CTA (pair) owns whole (row block, group) units of width/256 tiles,
 //                      sums each row's squares over the unit, and after the unit's last tile
 //                      normalizes / rotates the unit's columns in place from L2 while the MMA
-//                      runs ahead on the next unit (see norm_unit_pass).
+//                      runs ahead (see norm_pass_rows).
 //   kEpiResidual       out_f32 = C + (acc + bias) * gate    self-O (gate), cross-O (no gate),
 //   kEpiResidualLongK  (short / long K)                     FFN2 (gate)
 //                      and optionally a bf16 copy of out plus per-row (mean, M2) partials
@@ -89,7 +89,7 @@ template <>
 struct Cfg<kEpiNorm> {
   static constexpr int kStages = 4;
   static constexpr int kPairStages = 6;
-  // kEpiAct's staging + the two column halves' per-row sums of squares [2][128] fp32
+  // kEpiAct's staging + the per-row sums of squares of the two column halves [2][128] fp32
   static constexpr uint32_t kEpiBytes = 8 * 2 * kWarpStgBytes + 2 * BM * 4;
   static constexpr int kNumCBuf = 0;
   static constexpr int kEpiArrivals = 2 * kEpiThreads;
@@ -123,6 +123,10 @@ struct Cfg<kEpiResidualLongK> {
   static constexpr int kEpiArrivals = kEpiThreads;
 };
 
+template <int KIND>
+__host__ __device__ constexpr int num_threads() {
+  return kThreads;
+}
 template <int KIND, bool PAIR>
 __host__ __device__ constexpr int num_stages() {
   return PAIR ? Cfg<KIND>::kPairStages : Cfg<KIND>::kStages;
@@ -133,7 +137,8 @@ constexpr uint32_t smem_bytes() {
          Cfg<KIND>::kEpiBytes + 256 /*barriers + tmem slot*/;
 }
 static_assert(smem_bytes<kEpiAct, true>() <= 232448 && smem_bytes<kEpiResidualLongK, true>() <= 232448 &&
-                  smem_bytes<kEpiResidual, false>() <= 232448 && smem_bytes<kEpiNorm, true>() <= 232448,
+                  smem_bytes<kEpiResidual, false>() <= 232448 && smem_bytes<kEpiNorm, true>() <= 232448 &&
+                  smem_bytes<kEpiNorm, false>() <= 232448,
               "configuration exceeds the 227 KB shared-memory limit");
 
 // ---------------------------------------------------------------------------
@@ -179,43 +184,69 @@ __device__ __forceinline__ void ln_row_stats(const LnFold& ln, int row, float& m
   rstd = rsqrtf(m2 / static_cast<float>(ln.row_len) + ln.eps);
 }
 
-// In-place WanRMSNorm (+ RoPE) of one finished (row block, group) unit of the norm GEMM, run by
-// the eight epilogue warps after the unit's last tile: warp ew takes rows ew, ew + 8, ... of
-// the CTA's 128-row block; per row, lane l holds the 16-byte vectors at columns
-// 8 l + 256 u of the group, so its rotary pairs are the same four, (l % 16) * 4 .. + 3, in
-// every head (one float4 of cos and one of sin per row). The unit's bf16 GEMM output was
-// stored by TMA and is read back from L2 (ld.global.cg). Arithmetic of
+// In-place WanRMSNorm (+ RoPE) of rows [r0, r1) of one finished (row block, group) unit of the
+// norm GEMM, run by the eight epilogue warps: warp ew takes rows r0 + ew, r0 + ew + 8, ...,
+// kPassRows at a time (all their loads in flight together). Per row, lane l holds the 16-byte
+// vectors at columns 8 l + 256 u of the group, so its rotary pairs are the same four,
+// (l % 16) * 4 .. + 3, in every head (one float4 of cos and one of sin per row). The unit's bf16
+// GEMM output was stored by TMA and is read back from L2 (ld.global.cg). Arithmetic of
 // coda_wan/wan_coda_kernels.py:233-352 (_qk_rms_rope_kernel) and :371-411 (_rmsnorm_kernel):
 // rstd = rsqrt(mean(y^2) + eps) over the group's full width (y = the bf16 GEMM output),
-// z = bf16(bf16(y rstd) w), then (z_e cos - z_o sin, z_e sin + z_o cos) in fp32, one rounding.
-constexpr int kPassVec = 6;  // 16-byte vectors per lane in flight (one 1536-column row)
+// z = bf16(bf16(y rstd) w), then (z_e cos - z_o sin, z_e sin + z_o cos) in fp32, one rounding;
+// two columns per packed f32x2 instruction.
+constexpr int kPassVec = 6;   // 16-byte vectors per lane and row in flight (one 1536-column row)
+constexpr int kPassRows = 2;  // rows per warp in flight
 
-__device__ __forceinline__ void norm_unit_pass(const NormParams& np, const float* ss_x, int m_blk, int g, int M,
-                                               int rows_per_batch, int ew, int lane) {
+// bf16 rounding of a packed pair, back to a packed fp32 pair
+__device__ __forceinline__ uint64_t bf16_round2(uint64_t x) {
+  float a, b;
+  f2_unpack(x, a, b);
+  const float2 r = unpack_bf16x2(pack_bf16x2(a, b));
+  return f2_pack(r.x, r.y);
+}
+
+__device__ __forceinline__ void norm_pass_rows(const NormParams& np, const float* ss_x, int m_blk, int g, int M,
+                                               int rows_per_batch, int ew, int lane, int r0, int r1) {
   const float* wg = g == 0 ? np.w0 : np.w1;
   const bool rope = g < np.rope_groups;
+  const int rend = min(r1, M - m_blk * BM);  // rows past M hold no data
 #pragma unroll 1
-  for (int rr = ew; rr < BM; rr += 8) {
-    const int row = m_blk * BM + rr;
-    if (row >= M) break;
-    const float rstd = rsqrtf((ss_x[rr] + ss_x[BM + rr]) * np.inv_width + np.eps);
-    float cc[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
-    if (rope) {
-      const size_t tok = static_cast<size_t>(row % rows_per_batch + np.token_offset);
-      const float4 c4 = __ldg(reinterpret_cast<const float4*>(np.cos + tok * np.rope_ld) + (lane & 15));
-      const float4 s4 = __ldg(reinterpret_cast<const float4*>(np.sin + tok * np.rope_ld) + (lane & 15));
-      cc[0] = c4.x; cc[1] = c4.y; cc[2] = c4.z; cc[3] = c4.w;
-      sn[0] = s4.x; sn[1] = s4.y; sn[2] = s4.z; sn[3] = s4.w;
+  for (int rr0 = r0 + ew; rr0 < rend; rr0 += 8 * kPassRows) {
+    uint64_t rstd2[kPassRows];
+    uint64_t cs2[kPassRows][4], sc2[kPassRows][4];  // (cos, sin) and (sin, cos) of the lane's pairs
+    __nv_bfloat16* base[kPassRows];
+#pragma unroll
+    for (int j = 0; j < kPassRows; ++j) {
+      const int rr = min(rr0 + 8 * j, rend - 1);  // a clamped duplicate row is computed, not stored
+      const int row = m_blk * BM + rr;
+      const float rstd = rsqrtf((ss_x[rr] + ss_x[BM + rr]) * np.inv_width + np.eps);
+      rstd2[j] = f2_pack(rstd, rstd);
+      float cc[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+      if (rope) {
+        const size_t tok = static_cast<size_t>(row % rows_per_batch + np.token_offset);
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(np.cos + tok * np.rope_ld) + (lane & 15));
+        const float4 s4 = __ldg(reinterpret_cast<const float4*>(np.sin + tok * np.rope_ld) + (lane & 15));
+        cc[0] = c4.x; cc[1] = c4.y; cc[2] = c4.z; cc[3] = c4.w;
+        sn[0] = s4.x; sn[1] = s4.y; sn[2] = s4.z; sn[3] = s4.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        cs2[j][i] = f2_pack(cc[i], sn[i]);
+        sc2[j][i] = f2_pack(sn[i], cc[i]);
+      }
+      base[j] = reinterpret_cast<__nv_bfloat16*>(np.out) + static_cast<size_t>(row) * np.ldo +
+                static_cast<size_t>(g) * np.width;
     }
-    __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(np.out) + static_cast<size_t>(row) * np.ldo +
-                          static_cast<size_t>(g) * np.width;
 #pragma unroll 1
     for (int c0 = 0; c0 < np.width; c0 += 256 * kPassVec) {
-      uint4 raw[kPassVec];
+      uint4 raw[kPassRows][kPassVec];
 #pragma unroll
-      for (int u = 0; u < kPassVec; ++u) {
-        const int c = c0 + 256 * u + lane * 8;
-        if (c < np.width) raw[u] = ld_global_cg_v4(base + c);
+      for (int j = 0; j < kPassRows; ++j) {
+#pragma unroll
+        for (int u = 0; u < kPassVec; ++u) {
+          const int c = c0 + 256 * u + lane * 8;
+          if (c < np.width) raw[j][u] = ld_global_cg_v4(base[j] + c);
+        }
       }
 #pragma unroll
       for (int u = 0; u < kPassVec; ++u) {
@@ -223,28 +254,44 @@ __device__ __forceinline__ void norm_unit_pass(const NormParams& np, const float
         if (c >= np.width) break;
         const float4 wa = __ldg(reinterpret_cast<const float4*>(wg + c));
         const float4 wb = __ldg(reinterpret_cast<const float4*>(wg + c + 4));
-        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-        const uint32_t rw[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
-        float v[8];
+        const uint64_t w2[4] = {f2_pack(wa.x, wa.y), f2_pack(wa.z, wa.w), f2_pack(wb.x, wb.y), f2_pack(wb.z, wb.w)};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          v[2 * i] = __uint_as_float(rw[i] << 16);
-          v[2 * i + 1] = __uint_as_float(rw[i] & 0xFFFF0000u);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = bf16_round(bf16_round(v[i] * rstd) * wv[i]);
-        if (rope) {
+        for (int j = 0; j < kPassRows; ++j) {
+          if (rr0 + 8 * j >= rend) break;
+          const uint32_t rw[4] = {raw[j][u].x, raw[j][u].y, raw[j][u].z, raw[j][u].w};
+          uint32_t outw[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float e = v[2 * i], o = v[2 * i + 1];
-            v[2 * i] = e * cc[i] - o * sn[i];
-            v[2 * i + 1] = e * sn[i] + o * cc[i];
+            const float2 x = unpack_bf16x2(rw[i]);
+            const uint64_t y = bf16_round2(fmul2(f2_pack(x.x, x.y), rstd2[j]));
+            uint64_t z = bf16_round2(fmul2(y, w2[i]));
+            if (rope) {
+              float e, o;
+              f2_unpack(z, e, o);
+              // (e cos - o sin, e sin + o cos) = (e, e) * (cos, sin) + (-o, o) * (sin, cos)
+              z = ffma2(f2_pack(-o, o), sc2[j][i], fmul2(f2_pack(e, e), cs2[j][i]));
+            }
+            float a, b;
+            f2_unpack(z, a, b);
+            outw[i] = pack_bf16x2(a, b);
           }
+          st_global_v4(base[j] + c, outw[0], outw[1], outw[2], outw[3]);
         }
-        st_global_v4(base + c, pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                     pack_bf16x2(v[6], v[7]));
       }
     }
+  }
+}
+
+// Prefetch rows [r0, r1) of a finished unit's group columns into L2 (one 128-byte line per lane
+// and step), so that a later norm_pass_rows over them finds them there.
+__device__ __forceinline__ void norm_prefetch_rows(const NormParams& np, int m_blk, int g, int M, int ew, int lane,
+                                                   int r0, int r1) {
+  const int rend = min(r1, M - m_blk * BM);
+  const int row_bytes = np.width * 2;
+  for (int rr = r0 + ew; rr < rend; rr += 8) {
+    const char* base = reinterpret_cast<const char*>(np.out) +
+                       (static_cast<size_t>(m_blk * BM + rr) * np.ldo + static_cast<size_t>(g) * np.width) * 2;
+    for (int off = lane * 128; off < row_bytes; off += 32 * 128) prefetch_l2(base + off);
   }
 }
 
@@ -252,7 +299,7 @@ __device__ __forceinline__ void norm_unit_pass(const NormParams& np, const float
 // The kernel
 // ---------------------------------------------------------------------------
 template <int KIND, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(num_threads<KIND>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmC,
                 const __grid_constant__ CUtensorMap tmX, const GemmShape s, const EpiParams p) {
@@ -499,10 +546,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       // kEpiNorm: this thread's sum of squares of its row over the current unit's columns of
       // its half, and the two halves' sums exchanged at the end of each unit.
       uint64_t unit_ss2 = f2_pack(0.f, 0.f);
-      float* ss_x = reinterpret_cast<float*>(epi_base + 8 * 2 * kWarpStgBytes);
+      float* ss_x = reinterpret_cast<float*>(epi_base + 8 * 2 * kWarpStgBytes);  // [2][BM]
+      const uint64_t keep_policy = KIND == kEpiNorm ? l2_policy_evict_last() : 0ull;
+      // kEpiNorm: the last finished unit whose normalize pass is pending; it runs in slices of
+      // BM / unit_tiles rows, one after each following tile's epilogue, with the slice's rows
+      // prefetched into L2 when that tile's iteration starts.
+      int pend_mblk = -1, pend_g = 0, pend_slice = 0;
       for (int it = 0; it < my_count; ++it) {
         int m_blk, n_blk, upos;
         coords(it, m_blk, n_blk, upos);
+        if constexpr (KIND == kEpiNorm) {
+          if (pend_mblk >= 0)
+            norm_prefetch_rows(p.norm, pend_mblk, pend_g, s.M, ew, lane, pend_slice * BM / s.unit_tiles,
+                               (pend_slice + 1) * BM / s.unit_tiles);
+        }
         const int warp_row0 = m_blk * BM + wq * 32;
         const bool rows_any = warp_row0 < s.M;  // this warp's 32 rows hold data
         const int buf = it & 1;
@@ -591,16 +648,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (rows_any) tma_store_2d(&tmOut, stg_warp_ptr + sbuf * kWarpStgBytes, n0, warp_row0);
+            if (rows_any) {
+              if (KIND == kEpiNorm && ss_on) {  // read back by this CTA's normalize pass soon
+                tma_store_2d_hint(&tmOut, stg_warp_ptr + sbuf * kWarpStgBytes, n0, warp_row0, keep_policy);
+              } else {
+                tma_store_2d(&tmOut, stg_warp_ptr + sbuf * kWarpStgBytes, n0, warp_row0);
+              }
+            }
             bulk_commit();
           }
           sbuf ^= 1;
         }
         if constexpr (KIND == kEpiNorm) {
           unit_ss2 = ss2;
+          if (pend_mblk >= 0) {
+            norm_pass_rows(p.norm, ss_x, pend_mblk, pend_g, s.M, p.rows_per_batch, ew, lane,
+                           pend_slice * BM / s.unit_tiles, (pend_slice + 1) * BM / s.unit_tiles);
+            if (++pend_slice == s.unit_tiles) pend_mblk = -1;
+          }
           if (upos == s.unit_tiles - 1) {
-            // Unit done: merge the halves' sums, make this CTA's TMA stores of the unit visible
-            // to generic loads, and normalize / rotate the unit's columns in place.
+            // Unit done. The previous unit's last slice ran just above in every warp: wait for
+            // all of them before its sums of squares are overwritten. Then publish this unit's
+            // halves' sums and make this CTA's TMA stores of the unit visible to generic loads.
+            named_bar_sync(5, 2 * kEpiThreads);
             float s0, s1;
             f2_unpack(unit_ss2, s0, s1);
             ss_x[half * BM + r] = s0 + s1;
@@ -611,7 +681,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncwarp();
             named_bar_sync(5, 2 * kEpiThreads);
-            norm_unit_pass(p.norm, ss_x, m_blk, n_blk / s.unit_tiles, s.M, p.rows_per_batch, ew, lane);
+            pend_mblk = m_blk;
+            pend_g = n_blk / s.unit_tiles;
+            pend_slice = 0;
           }
         } else {
           if (ss_on && row_ok) {
@@ -620,6 +692,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             p.ss_part[static_cast<size_t>(row) * p.ss_ld + (nh >> 7)] = (s0 + s1) * (1.f / 128.f);
           }
         }
+      }
+      if constexpr (KIND == kEpiNorm) {
+        // the last unit's remaining rows (no tile left to hide them behind)
+        if (pend_mblk >= 0)
+          norm_pass_rows(p.norm, ss_x, pend_mblk, pend_g, s.M, p.rows_per_batch, ew, lane,
+                         pend_slice * BM / s.unit_tiles, BM);
       }
       if (lane == 0) bulk_wait_all<0>();
     } else if (half < Cfg<KIND>::kHalves) {
@@ -917,7 +995,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, con
   cudaGetDevice(&dev);
   constexpr uint32_t smem = smem_bytes<KIND, PAIR>();
   cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(num_threads<KIND>());
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

@@ -311,7 +311,7 @@ def test_gemm_norm_fused_equals_split(pkg, M, D, groups, rope, rpb, N_extra):
     cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
     kw = dict(vec=b, norm_groups=groups, norm_width=D, norm_w=(wq, wk if groups > 1 else None), norm_eps=1e-6,
               rope_groups=rope, rope_cos=cos if rope else None, rope_sin=sin if rope else None,
-              rows_per_batch=rpb, token_offset=5 if rope else 0)
+              rows_per_batch=rpb or M, token_offset=5 if rope else 0)
     split = pkg.ops.gemm_norm(a, w, fused=False, **kw)
     out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=DEV)
     fused = pkg.ops.gemm_norm(a, w, fused=True, out=out, **kw)

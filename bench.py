@@ -432,7 +432,10 @@ def run_ours(args) -> None:
                 "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside the long step)",
                 "launch_ms": ffn1_ms,
                 "flops_per_launch": k_flops,
-                "traffic": traffic_from_profiles("ffn1_gemm") if args.workload == "cfg3" else None,
+                # one ncu capture of the FFN1 launch at M = 65520 (1 GPU), scaled by the rows of
+                # this launch (A and the GELU output scale with the rows; the 27.5 MB weight does not)
+                "traffic": (traffic_from_profiles("ffn1_gemm") * (timer[0][2] / (2.0 * 65520 * w["ffn"] * w["dim"]))
+                            if args.workload == "cfg3" and timer and traffic_from_profiles("ffn1_gemm") else None),
             },
             "clocks": clk,
             "gpu_launches": launches,

@@ -21,13 +21,18 @@ def _port():
     return p
 
 
-def _inputs(cfg, dev):
+def _inputs(cfg, dev, padded=False):
     from oracle import wan_ref
 
-    return wan_ref.model_inputs(cfg, LATENT, 2, seed=5, device=dev)
+    inp = wan_ref.model_inputs(cfg, LATENT, 2, seed=5, device=dev)
+    if padded:
+        # second sample 2 x 8 x 10 = 160 tokens, padded to the first sample's 192: its padding
+        # keys must be masked on every rank (they land on rank 1 of 2)
+        inp["x"][1] = inp["x"][1][..., :LATENT[2] - 4].contiguous()
+    return inp
 
 
-def _worker(rank, world, port, root, transport, ret):
+def _worker(rank, world, port, root, transport, padded, ret):
     import sys
     from datetime import timedelta
 
@@ -44,7 +49,7 @@ def _worker(rank, world, port, root, transport, ret):
 
         pkg = load_package()
         cfg = wan_ref.WAN_1_3B
-        inp = _inputs(cfg, dev)
+        inp = _inputs(cfg, dev, padded)
         L = inp["seq_len"]
         sp = pkg.SeqParallel(dist.group.WORLD, world, rank, (LATENT[0], LATENT[1] // 2, LATENT[2] // 2), L,
                              transport=transport)
@@ -62,8 +67,8 @@ def _worker(rank, world, port, root, transport, ret):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["p2p", "nccl"])
-def test_sequence_parallel_matches_single_gpu(pkg, transport):
+@pytest.mark.parametrize("transport,padded", [("p2p", False), ("nccl", False), ("p2p", True), ("nccl", True)])
+def test_sequence_parallel_matches_single_gpu(pkg, transport, padded):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from pathlib import Path
@@ -73,13 +78,14 @@ def test_sequence_parallel_matches_single_gpu(pkg, transport):
     root = str(Path(__file__).resolve().parents[1])
     dev = torch.device("cuda", 0)
     cfg = wan_ref.WAN_1_3B
-    inp = _inputs(cfg, dev)
+    inp = _inputs(cfg, dev, padded)
     L = inp["seq_len"]
     params = pkg.build_wan(pkg.WAN_1_3B, seed=11, device=dev, num_layers=LAYERS)
     with torch.no_grad():
         full = pkg.FusedWanModel(params)(inp["x"], inp["t"], inp["context"], L, return_tokens=True).float().cpu()
     ret = mp.Manager().dict()
-    mp.start_processes(_worker, args=(2, _port(), root, transport, ret), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(2, _port(), root, transport, padded, ret), nprocs=2, start_method="spawn",
+                       join=True)
     Lp = L // 2
     for r in range(2):
         want = full[:, r * Lp:(r + 1) * Lp]

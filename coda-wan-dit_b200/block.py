@@ -231,14 +231,23 @@ class FusedWanBlock(nn.Module):
     def _carry(self) -> Carry:
         return self.carry if self.carry is not None else default_carry()
 
-    def _rope_tables(self, grid, freqs):
+    def _rope_tables(self, grid, freqs, rows: int):
+        """Token-major cos / sin tables of `grid` with at least `rows` rows: tokens past the grid
+        (padding up to the sequence length) get the identity rotation (cos 1, sin 0)."""
         if "given" in self._rope:
             return self._rope["given"]
-        key = (tuple(grid), freqs.data_ptr())
+        key = (tuple(grid), freqs.data_ptr(), rows)
         tab = self._rope.get(key)
         if tab is None:
-            tab = ops.build_wan_rope_table(grid, freqs)
-            self._rope = {key: tab}
+            cos, sin = ops.build_wan_rope_table(grid, freqs)
+            if cos.shape[0] < rows:
+                pad = rows - cos.shape[0]
+                cos = torch.cat([cos, cos.new_ones((pad, cos.shape[1]))])
+                sin = torch.cat([sin, sin.new_zeros((pad, sin.shape[1]))])
+            tab = (cos, sin)
+            if len(self._rope) > 8:
+                self._rope = {}
+            self._rope[key] = tab
         return tab
 
     def _input_stats(self, x2: torch.Tensor):
@@ -315,13 +324,19 @@ class FusedWanBlock(nn.Module):
             return ev[b, i * D:(i + 1) * D]
 
         # --- rope table rows for this (possibly token-sharded) block ---
+        # One table for all samples when they share a grid; otherwise each sample's rows are
+        # projected with its own grid's table (stock Wan applies each sample's own grid).
         if sp is not None:
             grid, token_offset, grid_rows_per_batch = sp.grid, sp.token_offset, L
+            sample_grids = None
+            cos, sin = self._rope_tables(grid, freqs, sp.seq_len)
         else:
-            grids = _host_values(grid_sizes)
-            grid = tuple(int(v) for v in grids[0])
+            grids = [tuple(int(v) for v in g) for g in _host_values(grid_sizes)]
             token_offset, grid_rows_per_batch = 0, L
-        cos, sin = self._rope_tables(grid, freqs)
+            sample_grids = grids if len(set(grids)) > 1 else None
+            if sample_grids is not None and len(sample_grids) != B:
+                raise ValueError(f"{len(sample_grids)} grid sizes for a batch of {B}")
+            cos, sin = self._rope_tables(grids[0], freqs, L)
 
         # --- self-attention branch ---
         qkv = torch.empty((M, 3 * D), dtype=torch.bfloat16, device=dev)
@@ -329,8 +344,11 @@ class FusedWanBlock(nn.Module):
         # kernel: the GEMM only emits the raw projection and its mean-square partials.
         fused_exchange = sp is not None and sp.fuses_qk_norm
         part = torch.empty((M, 2 * D // ops.RMS_BLOCK), dtype=torch.float32, device=dev) if fused_exchange else None
-        for b in range(Be):
-            r0, r1 = (0, M) if Be == 1 else (b * L, (b + 1) * L)
+        # QKV row segments: one per modulation row (Be) or, with per-sample grids, one per sample
+        nseg = B if sample_grids is not None else Be
+        for sg in range(nseg):
+            r0, r1 = (0, M) if nseg == 1 else (sg * L, (sg + 1) * L)
+            b = sg if Be > 1 else 0  # modulation row of this segment
             if folds is not None:
                 wf, cs, vec = folds[2 * b]
             else:
@@ -340,10 +358,11 @@ class FusedWanBlock(nn.Module):
             if fused_exchange:
                 ops.gemm_act(xb[r0:r1], wf, vec=vec, ln=ln, out=qkv[r0:r1], ms_out=part[r0:r1], ms_cols=2 * D)
                 continue
+            seg_cos, seg_sin = (cos, sin) if sample_grids is None else self._rope_tables(sample_grids[sg], freqs, L)
             ops.gemm_norm(
                 xb[r0:r1], wf, vec=vec, ln=ln, norm_groups=2, norm_width=D,
-                norm_w=(self.w_nq, self.w_nk), norm_eps=self.rms_eps, rope_groups=2, rope_cos=cos, rope_sin=sin,
-                rows_per_batch=grid_rows_per_batch, token_offset=token_offset, out=qkv[r0:r1],
+                norm_w=(self.w_nq, self.w_nk), norm_eps=self.rms_eps, rope_groups=2, rope_cos=seg_cos,
+                rope_sin=seg_sin, rows_per_batch=grid_rows_per_batch, token_offset=token_offset, out=qkv[r0:r1],
                 workspace=self.workspace,
             )
         if fused_exchange:

@@ -373,6 +373,8 @@ class FusedWanModel(nn.Module):
         sp = self.sp
         token_range = None if sp is None else (sp.token_offset, sp.token_offset + sp.local_len)
         x, grids, lens = self.embed_tokens(x_list, seq_len, token_range)
+        if sp is not None and any(tuple(g) != tuple(sp.grid) for g in grids):
+            raise ValueError(f"token sharding was set up for grid {tuple(sp.grid)}; the samples have grids {grids}")
         e, e0 = self.embed_time(t[:1] if shared_e else t)
         head_folds = self.prefold(e, e0, shared_e)
         context = self.embed_text(context_list, text_len)

@@ -161,6 +161,8 @@ class SeqParallel:
         P = self.world
         assert Lp == self.local_len and (B * H) % P == 0 and hd == 128
         assert qkv.stride(1) == 1 and part.stride(1) == 1 and cos.stride(1) == 1 and sin.stride() == cos.stride()
+        # the exchange reads the tables at global token positions up to P * Lp
+        assert cos.shape[0] >= P * Lp and sin.shape[0] >= P * Lp, "RoPE tables shorter than the sequence"
         if self._x is None or self._x.shape != (B, Lp, H, hd):
             if self._x is not None:
                 self.close()

@@ -197,3 +197,22 @@ def test_in_place_change_between_blocks_is_seen(pkg):
     g = run(f2, inp, freqs, x=g, ctx_dtype=torch.bfloat16)
     w = run(ref2, inp, freqs, x=w)
     assert rel_l2(g, w) <= 1e-2 and max_abs(g, w) <= 5e-2
+
+
+def test_model_forward_per_sample_grids_and_padding(pkg):
+    """CFG batch whose samples have different grids (2 x 8 x 12 and 2 x 8 x 10 tokens), both
+    padded to a 256-token sequence: each sample's q/k get its own grid's RoPE, padded keys are
+    masked. Three layers vs the fp32 oracle, which applies each sample's own grid."""
+    cfg = wan_ref.WAN_1_3B
+    ref = wan_ref.model_on_device(cfg, torch.float32, DEV, seed=35, num_layers=3)
+    params = pkg.build_wan(pkg.WAN_1_3B, seed=0, device=DEV, num_layers=3)
+    params.load_state_dict(ref.state_dict(), strict=True)
+    fused = pkg.FusedWanModel(params)
+    inp = wan_ref.model_inputs(cfg, (2, 16, 24), 2, seed=36, device=DEV)
+    inp["x"][1] = inp["x"][1][..., :20].contiguous()
+    with torch.no_grad():
+        want = ref(inp["x"], inp["t"], inp["context"], 256)
+        got = fused(inp["x"], inp["t"], inp["context"], 256)
+    assert [g.shape for g in got] == [w.shape for w in want]
+    for g, w in zip(got, want):
+        assert rel_l2(g, w) <= 2e-2

@@ -26,9 +26,9 @@ def _inputs(cfg, dev, padded=False):
 
     inp = wan_ref.model_inputs(cfg, LATENT, 2, seed=5, device=dev)
     if padded:
-        # second sample 2 x 8 x 10 = 160 tokens, padded to the first sample's 192: its padding
-        # keys must be masked on every rank (they land on rank 1 of 2)
-        inp["x"][1] = inp["x"][1][..., :LATENT[2] - 4].contiguous()
+        # both samples' 192 tokens padded to a 256-token sequence (as stock Wan pads to its
+        # fixed seq_len): the padding keys (on rank 1 of 2) must be masked on every rank
+        inp["seq_len"] = 256
     return inp
 
 

@@ -336,45 +336,45 @@ __global__ void __launch_bounds__(num_threads<KIND>(), 1)
     m_blk = PAIR ? 2 * mq + cta_rank : mq;
   };
   // This CTA's (pair's) tile sequence i = 0 .. my_count - 1 -> (m_blk, n_blk, upos).
-  // Plain kinds: tile t_first + i * t_step. kEpiNorm: first its units u = t_first + j * t_step
-  // (unit u = (row group u / norm_groups, group u % norm_groups), upos = tile index inside the
-  // unit), then a contiguous range of the plain tiles, sized so that every CTA (pair) ends up
-  // with at most ceil(all tiles / CTAs) tiles.
+  // Plain kinds: tile t_first + i * t_step. kEpiNorm: units u = t_first + j * t_step, unit u =
+  // (row group u / norm_groups, normalized group g = u % norm_groups): the group's unit_tiles
+  // tiles (upos = 0 .. unit_tiles - 1), then group g's share of the row group's plain tiles
+  // (upos = -1; the plain tiles of a row group are split evenly over its normalized groups, a
+  // remainder going to the groups (g + row group) % norm_groups < remainder), so that every
+  // tile of a row group runs at about the same time (its A rows are read from HBM once) and the
+  // normalize pass of a unit runs while its plain tiles are computed.
   int my_count = 0;
-  int seq_units = 0, seq_vstart = 0;
+  int seq_units = 0;
+  const int ng = KIND == kEpiNorm ? s.norm_groups : 1;
+  const int vbase = KIND == kEpiNorm ? s.plain_nblocks / ng : 0;
+  const int vrem = KIND == kEpiNorm ? s.plain_nblocks - vbase * ng : 0;
+  auto plain_count = [&](int g, int mq) { return vbase + ((g + mq) % ng < vrem ? 1 : 0); };
+  auto unit_len = [&](int u) { return s.unit_tiles + plain_count(u % ng, u / ng); };
   if constexpr (KIND == kEpiNorm) {
     const int G = t_step, c = t_first;
-    const int base = s.units / G, rem = s.units - (s.units / G) * G;
-    seq_units = base + (c < rem ? 1 : 0);
-    const int mg = s.units / s.norm_groups;
-    const int P = mg * s.plain_nblocks;
-    const int T = (s.units * s.unit_tiles + P + G - 1) / G;
-    const int v1 = max(0, T - s.unit_tiles * (base + 1));
-    const int v0 = max(0, T - s.unit_tiles * base);
-    int vs = min(c, rem) * v1 + max(0, c - rem) * v0;
-    int ve = vs + (c < rem ? v1 : v0);
-    vs = min(vs, P);
-    ve = min(ve, P);
-    seq_vstart = vs;
-    my_count = seq_units * s.unit_tiles + (ve - vs);
+    seq_units = s.units / G + (c < s.units - (s.units / G) * G ? 1 : 0);
+    for (int j = 0; j < seq_units; ++j) my_count += unit_len(t_first + j * t_step);
   } else {
     my_count = t_first < s.tiles ? (s.tiles - 1 - t_first) / t_step + 1 : 0;
   }
   auto coords = [&](int i, int& m_blk, int& n_blk, int& upos) {
     if constexpr (KIND == kEpiNorm) {
-      int mq;
-      const int nu = seq_units * s.unit_tiles;
-      if (i < nu) {
-        const int j = i / s.unit_tiles;
-        upos = i - j * s.unit_tiles;
-        const int u = t_first + j * t_step;
-        mq = u / s.norm_groups;
-        n_blk = (u - mq * s.norm_groups) * s.unit_tiles + upos;
+      int u = t_first, len = unit_len(u);
+      while (i >= len) {  // walk to the unit holding position i (a few units per CTA)
+        i -= len;
+        u += t_step;
+        len = unit_len(u);
+      }
+      const int mq = u / ng;
+      const int g = u - mq * ng;
+      if (i < s.unit_tiles) {
+        upos = i;
+        n_blk = g * s.unit_tiles + i;
       } else {
-        const int pidx = seq_vstart + (i - nu);
-        mq = pidx / s.plain_nblocks;
-        n_blk = s.norm_groups * s.unit_tiles + (pidx - mq * s.plain_nblocks);
         upos = -1;
+        int v0 = 0;  // this group's first plain tile of the row group: the lower groups' shares
+        for (int g2 = 0; g2 < g; ++g2) v0 += plain_count(g2, mq);
+        n_blk = ng * s.unit_tiles + v0 + (i - s.unit_tiles);
       }
       m_blk = PAIR ? 2 * mq + cta_rank : mq;
     } else {

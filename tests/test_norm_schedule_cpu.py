@@ -1,43 +1,35 @@
 """The tile schedule of the one-launch norm GEMM (kEpiNorm in csrc/gemm.cu), restated in Python:
-every (row block, N tile) is visited exactly once, each CTA (pair) gets whole (row block, group)
-units first and then a contiguous range of the plain tiles, and no CTA gets more than
-ceil(tiles / CTAs) + the unit remainder. The GPU test test_gemm_norm_fused_equals_split checks
-the kernel's output on the same shapes; this checks the arithmetic for many more grids."""
+every (row block, N tile) is visited exactly once; each CTA (pair) takes (row group, normalized
+group) units u = c, c + CTAs, ..., each being the group's N tiles in order followed by the
+group's even share of that row group's plain tiles (a remainder rotating over the groups with
+the row group); when the plain tiles split evenly (all Wan shapes) the busiest CTA gets at
+most one unit more than the average. The GPU test test_gemm_norm_fused_equals_split checks the kernel's output on
+the same shapes; this checks the arithmetic for many more grids."""
 import itertools
 
 import pytest
 
 
 def schedule(m_blocks, n_blocks, norm_groups, unit_tiles, pair, grid):
-    """Mirror of the kernel's per-CTA sequence (gemm.cu, `coords` for kEpiNorm)."""
+    """Mirror of the kernel's per-CTA sequence (gemm.cu, `coords` for kEpiNorm): a list of
+    (row group, N tile, position inside the unit or -1) per CTA (pair)."""
     mg = (m_blocks + 1) // 2 if pair else m_blocks
     units = mg * norm_groups
     plain = n_blocks - norm_groups * unit_tiles
+    vbase, vrem = divmod(plain, norm_groups)
     G = grid // 2 if pair else grid
     out = {}
     for c in range(G):
-        base, rem = units // G, units % G
-        su = base + (1 if c < rem else 0)
-        P = mg * plain
-        T = (units * unit_tiles + P + G - 1) // G
-        v1 = max(0, T - unit_tiles * (base + 1))
-        v0 = max(0, T - unit_tiles * base)
-        vs = min(c, rem) * v1 + max(0, c - rem) * v0
-        ve = min(vs + (v1 if c < rem else v0), P)
-        vs = min(vs, P)
         seq = []
-        for i in range(su * unit_tiles + (ve - vs)):
-            nu = su * unit_tiles
-            if i < nu:
-                j, up = divmod(i, unit_tiles)
-                u = c + j * G
-                mq = u // norm_groups
-                nb = (u - mq * norm_groups) * unit_tiles + up
-            else:
-                pidx = vs + (i - nu)
-                mq, nb = divmod(pidx, plain)
-                nb += norm_groups * unit_tiles
-            seq.append((mq, nb))
+        for u in range(c, units, G):
+            mq, g = divmod(u, norm_groups)
+            seq += [(mq, g * unit_tiles + k, k) for k in range(unit_tiles)]
+
+            def count(g2):
+                return vbase + (1 if (g2 + mq) % norm_groups < vrem else 0)
+
+            v0 = norm_groups * unit_tiles + sum(count(g2) for g2 in range(g))
+            seq += [(mq, v0 + k, -1) for k in range(count(g))]
         out[c] = seq
     return out, mg
 
@@ -52,17 +44,24 @@ def test_every_tile_once_and_units_whole(M, N, groups, width, pair, grid):
     m_blocks, n_blocks = (M + 127) // 128, (N + 255) // 256
     tpu = width // 256
     seqs, mg = schedule(m_blocks, n_blocks, groups, tpu, pair, grid)
-    flat = [t for s in seqs.values() for t in s]
+    flat = [t[:2] for s in seqs.values() for t in s]
     assert sorted(flat) == sorted(itertools.product(range(mg), range(n_blocks)))
     for s in seqs.values():
-        # units first: each normalized group's tiles of one row block come consecutively, in order
+        # a unit: the group's tiles of one row group in order, then plain tiles of the same row group
         k = 0
-        while k < len(s) and s[k][1] < groups * tpu:
+        while k < len(s):
+            assert s[k][2] == 0
             unit = s[k:k + tpu]
+            assert [t[2] for t in unit] == list(range(tpu)) and len({t[0] for t in unit}) == 1
             assert [t[1] for t in unit] == list(range(unit[0][1], unit[0][1] + tpu))
-            assert unit[0][1] % tpu == 0 and len({t[0] for t in unit}) == 1
             k += tpu
-        assert all(t[1] >= groups * tpu for t in s[k:])  # then plain tiles only
+            while k < len(s) and s[k][2] == -1:
+                assert s[k][0] == unit[0][0] and s[k][1] >= groups * tpu
+                k += 1
+    loads = [len(s) for s in seqs.values()]
+    per_unit = tpu + -(-(n_blocks - groups * tpu) // groups)
+    if (n_blocks - groups * tpu) % groups == 0:  # every unit equally long (all Wan shapes)
+        assert max(loads) <= -(-len(flat) // len(loads)) + per_unit
 
 
 def test_tail_of_the_cfg3_qkv_schedule():

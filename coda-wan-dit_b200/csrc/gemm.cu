@@ -4,7 +4,7 @@
 //                                       fp32 accumulation in TMEM.
 //
 // CTA = 10 warps (320 threads), one CTA per SM, grid = the co-resident CTA count, static tile order
-// tile -> (m_blk = tile / n_blocks, n_blk = tile % n_blocks):
+// tile -> (m_blk, n_blk) row-major, or in groups of 8 row blocks for a large B (tile_coords):
 //   warp 0     TMA producer: A (128x64) and B (256x64) tiles, 128-byte swizzle,
 //              STAGES-deep shared-memory ring (full/empty mbarriers).
 //   warp 1     TMEM allocator (512 columns = two 128x256 fp32 accumulators) and
@@ -72,6 +72,8 @@ constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 // of A and one 128-row half of B, and holds its 128 accumulator rows in its own TMEM.
 constexpr uint32_t kPairStageBytes = kTileABytes + kTileBBytes / 2;  // 32 KB
 constexpr int kTmemCols = 2 * BN;  // two accumulator buffers
+constexpr int kRasterRows = 8;     // row blocks per rasterization group for a large B (tile_coords)
+constexpr long long kRasterBBytes = 64ll << 20;  // B operands above this get grouped rasterization
 enum EpiKind { kEpiAct = 0, kEpiResidual = 1, kEpiResidualLongK = 3, kEpiNorm = 4 };
 
 template <int KIND>
@@ -324,15 +326,27 @@ __global__ void __launch_bounds__(num_threads<KIND>(), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Tile schedule. 1-CTA: tile t -> (m_blk, n_blk) = (t / n_blocks, t % n_blocks), CTA b takes
-  // t = b, b + grid, ... Pair: s.tiles counts 256-row pair tiles; pair c = blockIdx / 2 takes
-  // t = c, c + grid/2, ... and CTA rank r of the pair owns 128-row block 2 (t / n_blocks) + r.
+  // Tile schedule. 1-CTA: CTA b takes tiles t = b, b + grid, ... (tile_coords maps t to a row
+  // block and an N block). Pair: s.tiles counts 256-row pair tiles; pair c = blockIdx / 2 takes
+  // t = c, c + grid/2, ... and CTA rank r of the pair owns 128-row block 2 mq + r of pair row mq.
   const int cta_rank = PAIR ? static_cast<int>(cluster_ctarank()) : 0;
   const int t_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int t_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  // Rasterization: tiles run in groups of s.raster_rows row blocks (256-row pair blocks for
+  // pairs), row-minor inside a group. raster_rows = 1 is the plain row-major order (a row
+  // block's N blocks in turn: its A rows stay hot while the whole B is L2-resident). For a B
+  // larger than L2 (the 14B layers: 142-157 MB) the host picks groups of kRasterRows: the tiles
+  // in flight then share a few row blocks of A and a few column blocks of B, and B is read from
+  // HBM about once per group instead of once per row block.
   auto tile_coords = [&](int t, int& m_blk, int& n_blk) {
-    const int mq = t / s.n_blocks;
-    n_blk = t - mq * s.n_blocks;
+    const int mg = PAIR ? (s.m_blocks + 1) / 2 : s.m_blocks;
+    const int per_group = s.raster_rows * s.n_blocks;
+    const int grp = t / per_group;
+    const int first = grp * s.raster_rows;
+    const int gm = min(s.raster_rows, mg - first);
+    const int r = t - grp * per_group;
+    n_blk = r / gm;
+    const int mq = first + (r - n_blk * gm);
     m_blk = PAIR ? 2 * mq + cta_rank : mq;
   };
   // This CTA's (pair's) tile sequence i = 0 .. my_count - 1 -> (m_blk, n_blk, upos).
@@ -1049,6 +1063,7 @@ GemmShape make_shape(int M, int N, int K) {
   s.M = M;
   s.N = N;
   s.K = K;
+  s.raster_rows = static_cast<long long>(N) * K * 2 > kRasterBBytes ? kRasterRows : 1;
   s.m_blocks = (M + BM - 1) / BM;
   s.n_blocks = (N + BN - 1) / BN;
   s.k_blocks = (K + BK - 1) / BK;

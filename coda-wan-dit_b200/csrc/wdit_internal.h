@@ -11,6 +11,7 @@ struct GemmShape {
   // groups of `unit_tiles` N tiles each are processed one (row block, group) unit at a time by
   // one CTA (pair); the remaining `plain_nblocks` N tiles of every row block are plain tiles.
   int norm_groups, unit_tiles, plain_nblocks, units;
+  int raster_rows;  // row blocks per rasterization group (1 = row-major tile order)
 };
 
 // Full-width RMSNorm (+ RoPE) applied by the norm GEMM's epilogue (kEpiNorm).

@@ -1,6 +1,6 @@
 """Config 2: isolated fused-GEMM microbenchmark on one B200 (plus the memory-bound passes).
 
-    python microbench.py [--m 32760] [--only ffn1,ffn2,...] [--iters 20]
+    python microbench.py [--m 32760] [--only ffn1,ffn2,...] [--iters 20] [--model 1.3b|14b]
 
 Each kernel is timed alone with CUDA events (median of --iters launches after warm-up; the
 operands exceed the 126 MB L2 at the default M, so launches do not hit in L2 from the
@@ -18,6 +18,7 @@ Shapes (Wan2.1-1.3B, batch 1, N = 32760 tokens):
   cross_o[M x 1536] . [1536 x 1536]  bias + residual (+ bf16 copy + stats)
   stats  LayerNorm statistics pass over fp32 [M x 1536]   (reads 4 B, writes 8 B per row... HBM)
   fold   per-step weight fold of the FFN1 weight [8960 x 1536] (reads 2 B + writes 2 B / weight)
+(`--model 14b`: the same kernels at the Wan2.1-14B shapes, dim 5120 and ffn 13824.)
 """
 from __future__ import annotations
 
@@ -63,11 +64,15 @@ def _time(fn, iters: int, warmup: int = 3) -> float:
     return statistics.median(out)
 
 
-def run(M: int = 32760, only: set[str] | None = None, iters: int = 20, cublas: bool = True) -> list[dict]:
+SHAPES = {"1.3b": (1536, 8960), "14b": (5120, 13824)}  # (dim, ffn_dim)
+
+
+def run(M: int = 32760, only: set[str] | None = None, iters: int = 20, cublas: bool = True,
+        model: str = "1.3b") -> list[dict]:
     pkg = _pkg()
     ops = pkg.ops
     dev = torch.device("cuda")
-    D, F = 1536, 8960
+    D, F = SHAPES[model]
     g = torch.Generator(device="cpu").manual_seed(0)
 
     def rnd(shape, scale=1.0, dtype=torch.bfloat16):
@@ -80,7 +85,7 @@ def run(M: int = 32760, only: set[str] | None = None, iters: int = 20, cublas: b
     res = []
 
     def add(name, ms, flops=None, nbytes=None, cublas_ms=None):
-        row = {"kernel": name, "M": M, "ms": ms}
+        row = {"kernel": name, "model": model, "M": M, "ms": ms}
         if flops:
             row["tflops"] = flops / (ms * 1e-3) / 1e12
             row["frac_of_peak"] = row["tflops"] / peak_tf
@@ -185,10 +190,12 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--pair", type=int, default=1, help="CTA pairs for the tensor-bound GEMMs (1) or not (0)")
+    ap.add_argument("--model", choices=tuple(SHAPES), default="1.3b",
+                    help="layer shapes: Wan2.1-1.3B (dim 1536, ffn 8960) or 14B (dim 5120, ffn 13824)")
     a = ap.parse_args()
     only = set(a.only.split(",")) if a.only else None
     _pkg()._lib.load().wdit_set_cta_pair(a.pair)
-    run(a.m, only, a.iters, not a.no_cublas)
+    run(a.m, only, a.iters, not a.no_cublas, a.model)
 
 
 if __name__ == "__main__":

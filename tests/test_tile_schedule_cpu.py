@@ -1,4 +1,4 @@
-"""The tile schedule of the one-launch norm GEMM (kEpiNorm in csrc/gemm.cu), restated in Python:
+"""Tile schedules of csrc/gemm.cu restated in Python. The one-launch norm GEMM (kEpiNorm):
 every (row block, N tile) is visited exactly once; each CTA (pair) takes (row group, normalized
 group) units u = c, c + CTAs, ..., each being the group's N tiles in order followed by the
 group's even share of that row group's plain tiles (a remainder rotating over the groups with
@@ -68,3 +68,35 @@ def test_tail_of_the_cfg3_qkv_schedule():
     """cfg3 QKV on 74 CTA pairs: at most 63 tiles per pair against 62.3 on average."""
     seqs, _ = schedule(512, 18, 2, 6, True, 148)
     assert max(len(s) for s in seqs.values()) == 63
+
+
+def raster(t, mg, n_blocks, group=8):
+    """Mirror of gemm.cu's tile_coords: tile t -> (row block, N block), groups of `group` row
+    blocks, row-minor inside a group (group 1: row-major)."""
+    per = group * n_blocks
+    grp = t // per
+    first = grp * group
+    gm = min(group, mg - first)
+    r = t - grp * per
+    n = r // gm
+    return first + (r - n * gm), n
+
+
+@pytest.mark.parametrize("group", [1, 8])
+@pytest.mark.parametrize("mg", [1, 2, 7, 8, 9, 17, 32, 256, 591])
+@pytest.mark.parametrize("n_blocks", [1, 6, 18, 35, 54, 60])
+def test_grouped_rasterization_is_a_permutation(mg, n_blocks, group):
+    tiles = [raster(t, mg, n_blocks, group) for t in range(mg * n_blocks)]
+    assert sorted(tiles) == sorted(itertools.product(range(mg), range(n_blocks)))
+    if group == 1:
+        assert tiles == [divmod(t, n_blocks) for t in range(mg * n_blocks)]  # row-major
+
+
+def test_grouped_rasterization_bounds_the_tiles_in_flight():
+    """74 CTA pairs working on consecutive tiles of the 14B FFN1 at M = 151200 (591 pair row
+    blocks x 54 N blocks) touch at most 8 row blocks and 10 N blocks at a time, so the weight
+    columns in flight (10 x 2.6 MB) and the A rows (8 x 2.6 MB) fit in L2 together."""
+    mg, nb = 591, 54
+    for start in range(0, mg * nb - 74, 997):
+        window = [raster(t, mg, nb) for t in range(start, start + 74)]
+        assert len({m for m, _ in window}) <= 16 and len({n for _, n in window}) <= 11

@@ -306,7 +306,7 @@ def run_ours(args) -> None:
     sp = None
     if world > 1:
         sp = pkg.SeqParallel(dist.group.WORLD, world, rank, (latent[1], latent[2] // 2, latent[3] // 2), L,
-                             transport=args.transport)
+                             transport=args.transport, gemm_exchange=args.gemm_exchange)
     torch.manual_seed(SEED)
     params = pkg.build_wan(getattr(pkg, w["shape"]), seed=SEED, device=dev, num_layers=layers)
     # The weights as built (before the fused blocks re-point the parameters at packed storage),
@@ -416,8 +416,9 @@ def run_ours(args) -> None:
             "config": {"workload": w["name"],
                        "weights": "random init", "layers": layers, "global_batch": BATCH,
                        "seq_len": L, "latent": list(latent), "context": list(TEXT), "t": T_STEP,
-                       "parallelism": (f"sp{world} (token-sharded, Ulysses all-to-all over {args.transport})"
-                                       if world > 1 else "single GPU"),
+                       "parallelism": (f"sp{world} (token-sharded, Ulysses all-to-all over {args.transport}"
+                                       + (", sent by the QKV GEMM" if sp is not None and sp.gemm_exchange else "")
+                                       + ")" if world > 1 else "single GPU"),
                        "attention": "torch SDPA (out of scope)", "l2": "activations > L2 (no flush needed)"},
             "tflops": fl["total"] / (ms * 1e-3) / 1e12,
             "gemm_tflop_per_step": fl["gemm"] / 1e12,
@@ -487,6 +488,9 @@ def main():
     ap.add_argument("--oracle-iters", type=int, default=5)
     ap.add_argument("--transport", choices=("p2p", "nccl"), default="p2p",
                     help="Ulysses all-to-all: NVLink peer stores (p2p) or NCCL all_to_all_single")
+    ap.add_argument("--gemm-exchange", action="store_true",
+                    help="p2p: the QKV GEMM stores q / k / v into the peers itself instead of a separate "
+                         "exchange kernel after it (slower on B200, kept as an option)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

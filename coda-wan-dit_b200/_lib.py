@@ -62,6 +62,11 @@ _SIGNATURES = {
         c_int,
         [P, I, P, I, P, I, I, I, I, P, P, P, I, I, F, I, I, P, P, F, I, P, P, I, I, I, P, I],
     ),
+    "wdit_gemm_norm_exchange": (
+        c_int,
+        [P, I, P, I, P, I, I, I, P, P, P, I, I, F, P, P, F, P, P, I, I, I, I, I, I, P, c_longlong, c_longlong,
+         c_uint, P, P, I],
+    ),
     "wdit_gemm_norm_static": (
         c_int,
         [P, I, P, I, P, I, I, I, I, P, P, P, I, I, F, I, I, P, P, F, I, P, P, I, I, I, P, I],
@@ -143,7 +148,8 @@ def check(rc: int, what: str) -> None:
 
 # Entry points that launch device work (counted by launch_counter for the benchmark).
 _LAUNCHING = {
-    "wdit_gemm_act", "wdit_gemm_residual", "wdit_gemm_norm", "wdit_gemm_norm_fused", "wdit_ln_stats",
+    "wdit_gemm_act", "wdit_gemm_residual", "wdit_gemm_norm", "wdit_gemm_norm_fused", "wdit_gemm_norm_exchange",
+    "wdit_ln_stats",
     "wdit_fold_weight",
     "wdit_fold_weight_batch", "wdit_rms_apply_layers", "wdit_patch_rows",
     "wdit_layernorm_modulation", "wdit_rmsnorm", "wdit_qk_rms_rope_from_partials", "wdit_rope_table",

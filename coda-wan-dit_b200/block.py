@@ -339,13 +339,26 @@ class FusedWanBlock(nn.Module):
             cos, sin = self._rope_tables(grids[0], freqs, L)
 
         # --- self-attention branch ---
-        qkv = torch.empty((M, 3 * D), dtype=torch.bfloat16, device=dev)
-        # With the NVLink peer-store exchange the q/k RMSNorm + RoPE happen inside the exchange
-        # kernel: the GEMM only emits the raw projection and its mean-square partials.
-        fused_exchange = sp is not None and sp.fuses_qk_norm
-        part = torch.empty((M, 2 * D // ops.RMS_BLOCK), dtype=torch.float32, device=dev) if fused_exchange else None
         # QKV row segments: one per modulation row (Be) or, with per-sample grids, one per sample
         nseg = B if sample_grids is not None else Be
+        # With the NVLink peer-store exchange the q/k RMSNorm + RoPE happen inside the exchange:
+        # either the QKV GEMM stores into the owners' regions itself (one segment), or the GEMM
+        # only emits the raw projection and its mean-square partials for the exchange kernel.
+        fused_exchange = sp is not None and sp.fuses_qk_norm
+        gemm_exchange = fused_exchange and sp.gemm_exchange and nseg == 1 and D % 256 == 0
+        if gemm_exchange:
+            nseg = 0
+            if folds is not None:
+                wf, cs, vec = folds[0]
+            else:
+                wf, cs, vec = ops.fold_weight(self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=e_row(0, 1),
+                                              shift_a=mod[0], shift_b=e_row(0, 0), bias=self.b_qkv)
+            y = sp.self_attention_gemm(xb, wf, vec, ops.LnFold(cs, stats, self.eps), self.w_nq, self.w_nk,
+                                       self.rms_eps, cos, sin, B, L, H, hd, key_lens=_host_values(seq_lens))
+        else:
+            qkv = torch.empty((M, 3 * D), dtype=torch.bfloat16, device=dev)
+        part = torch.empty((M, 2 * D // ops.RMS_BLOCK), dtype=torch.float32, device=dev) \
+            if fused_exchange and not gemm_exchange else None
         for sg in range(nseg):
             r0, r1 = (0, M) if nseg == 1 else (sg * L, (sg + 1) * L)
             b = sg if Be > 1 else 0  # modulation row of this segment
@@ -365,7 +378,9 @@ class FusedWanBlock(nn.Module):
                 rope_sin=seg_sin, rows_per_batch=grid_rows_per_batch, token_offset=token_offset, out=qkv[r0:r1],
                 workspace=self.workspace,
             )
-        if fused_exchange:
+        if gemm_exchange:
+            pass  # y came from the exchanging GEMM
+        elif fused_exchange:
             y = sp.self_attention_p2p(qkv, part, self.w_nq, self.w_nk, self.rms_eps, cos, sin, B, L, H, hd,
                                       key_lens=_host_values(seq_lens))
         elif sp is not None:

@@ -207,16 +207,30 @@ __device__ __forceinline__ uint64_t bf16_round2(uint64_t x) {
   return f2_pack(r.x, r.y);
 }
 
-__device__ __forceinline__ void norm_pass_rows(const NormParams& np, const float* ss_x, int m_blk, int g, int M,
-                                               int rows_per_batch, int ew, int lane, int r0, int r1) {
+// Address in the exchange region of the rank owning unit (b, head of column c) for matrix mat
+// (0 q, 1 k, 2 v), global token gtok, column c of the matrix (c % 128 inside the head).
+__device__ __forceinline__ unsigned char* xchg_addr(const XchgParams& xc, int mat, int b, int gtok, int c) {
+  const int h = c >> 7;
+  const int u = b * xc.H + h;
+  const int pr = u / xc.U;
+  const int ul = u - pr * xc.U;
+  return xc.base[pr] + xc.full_off +
+         ((((static_cast<long long>(mat) * xc.U + ul) * xc.L + gtok) * 128 + (c & 127)) * 2);
+}
+
+__device__ __forceinline__ void norm_pass_rows(const NormParams& np, const XchgParams& xc, const float* ss_x,
+                                               int m_blk, int g, int M, int rows_per_batch, int ew, int lane,
+                                               int r0, int r1) {
   const float* wg = g == 0 ? np.w0 : np.w1;
   const bool rope = g < np.rope_groups;
+  const bool remote = xc.P > 0;  // results go to the owners' exchange regions, not in place
   const int rend = min(r1, M - m_blk * BM);  // rows past M hold no data
 #pragma unroll 1
   for (int rr0 = r0 + ew; rr0 < rend; rr0 += 8 * kPassRows) {
     uint64_t rstd2[kPassRows];
     uint64_t cs2[kPassRows][4], sc2[kPassRows][4];  // (cos, sin) and (sin, cos) of the lane's pairs
     __nv_bfloat16* base[kPassRows];
+    int xb[kPassRows], xtok[kPassRows];  // remote: batch entry and global token of the row
 #pragma unroll
     for (int j = 0; j < kPassRows; ++j) {
       const int rr = min(rr0 + 8 * j, rend - 1);  // a clamped duplicate row is computed, not stored
@@ -238,6 +252,8 @@ __device__ __forceinline__ void norm_pass_rows(const NormParams& np, const float
       }
       base[j] = reinterpret_cast<__nv_bfloat16*>(np.out) + static_cast<size_t>(row) * np.ldo +
                 static_cast<size_t>(g) * np.width;
+      xb[j] = remote ? row / xc.Lp : 0;
+      xtok[j] = remote ? xc.rank * xc.Lp + (row - xb[j] * xc.Lp) : 0;
     }
 #pragma unroll 1
     for (int c0 = 0; c0 < np.width; c0 += 256 * kPassVec) {
@@ -277,7 +293,9 @@ __device__ __forceinline__ void norm_pass_rows(const NormParams& np, const float
             f2_unpack(z, a, b);
             outw[i] = pack_bf16x2(a, b);
           }
-          st_global_v4(base[j] + c, outw[0], outw[1], outw[2], outw[3]);
+          void* dst = remote ? static_cast<void*>(xchg_addr(xc, g, xb[j], xtok[j], c))
+                             : static_cast<void*>(base[j] + c);
+          st_global_v4(dst, outw[0], outw[1], outw[2], outw[3]);
         }
       }
     }
@@ -651,6 +669,19 @@ __global__ void __launch_bounds__(num_threads<KIND>(), 1)
               ss2 = ffma2(f2, f2, ss2);
             }
           }
+          if (KIND == kEpiNorm && upos < 0 && p.xchg.P > 0) {
+            // Token-sharded run: a plain (v) tile goes straight from registers into the exchange
+            // region of the rank owning its unit, 64 contiguous bytes per row.
+            if (row_ok) {
+              const XchgParams& xc = p.xchg;
+              const int b = row / xc.Lp;
+              const int gtok = xc.rank * xc.Lp + (row - b * xc.Lp);
+              unsigned char* dst = xchg_addr(xc, 2, b, gtok, n0 - s.norm_groups * p.norm.width);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) st_global_v4(dst + 16 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+            }
+            continue;
+          }
           // Stage the warp's 32 rows x 32 bf16 (64-byte swizzle) and store them with TMA.
           if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
           __syncwarp();
@@ -676,7 +707,7 @@ __global__ void __launch_bounds__(num_threads<KIND>(), 1)
         if constexpr (KIND == kEpiNorm) {
           unit_ss2 = ss2;
           if (pend_mblk >= 0) {
-            norm_pass_rows(p.norm, ss_x, pend_mblk, pend_g, s.M, p.rows_per_batch, ew, lane,
+            norm_pass_rows(p.norm, p.xchg, ss_x, pend_mblk, pend_g, s.M, p.rows_per_batch, ew, lane,
                            pend_slice * BM / s.unit_tiles, (pend_slice + 1) * BM / s.unit_tiles);
             if (++pend_slice == s.unit_tiles) pend_mblk = -1;
           }
@@ -710,7 +741,7 @@ __global__ void __launch_bounds__(num_threads<KIND>(), 1)
       if constexpr (KIND == kEpiNorm) {
         // the last unit's remaining rows (no tile left to hide them behind)
         if (pend_mblk >= 0)
-          norm_pass_rows(p.norm, ss_x, pend_mblk, pend_g, s.M, p.rows_per_batch, ew, lane,
+          norm_pass_rows(p.norm, p.xchg, ss_x, pend_mblk, pend_g, s.M, p.rows_per_batch, ew, lane,
                          pend_slice * BM / s.unit_tiles, BM);
       }
       if (lane == 0) bulk_wait_all<0>();
@@ -916,11 +947,29 @@ __global__ void __launch_bounds__(num_threads<KIND>(), 1)
     }
   }
 
+  if constexpr (KIND == kEpiNorm) {
+    if (p.xchg.P > 0) __threadfence_system();  // this thread's stores into peer regions are visible
+  }
   tc_fence_before();
   if constexpr (PAIR) {
     cluster_sync_all();  // neither CTA leaves while the other may still signal or read it
   } else {
     __syncthreads();
+  }
+  if constexpr (KIND == kEpiNorm) {
+    // The last CTA to finish publishes the exchange epoch into flags[rank] of every region
+    // (system-scope release), after which the owners may read what this rank stored.
+    if (p.xchg.P > 0 && threadIdx.x == 0) {
+      const XchgParams& xc = p.xchg;
+      if (atomicAdd(xc.done_ctr, 1u) == gridDim.x - 1) {
+        __threadfence_system();
+        for (int q = 0; q < xc.P; ++q) {
+          unsigned int* f = reinterpret_cast<unsigned int*>(xc.base[q] + xc.flag_off) + xc.rank;
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(xc.epoch) : "memory");
+        }
+        atomicExch(xc.done_ctr, 0u);
+      }
+    }
   }
   if (warp == 1) {
     __syncwarp();
@@ -1170,8 +1219,9 @@ int run_norm_fused(const void* A, int lda, const void* B, int ldb, void* out, in
                    int ln_stats_width, float ln_eps, int norm_groups, int norm_width, const float* norm_w0,
                    const float* norm_w1, float norm_eps, int rope_groups, const float* rope_cos,
                    const float* rope_sin, int rope_ld, int rows_per_batch, int token_offset, cudaStream_t stream,
-                   int max_ctas) {
+                   int max_ctas, const XchgParams* xchg = nullptr) {
   EpiParams p = {};
+  if (xchg != nullptr) p.xchg = *xchg;
   int rc = ln_fill(&p.ln, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width, K, ln_eps);
   if (rc) return rc;
   p.vec = vec;
@@ -1401,6 +1451,46 @@ int wdit_gemm_norm_fused(const void* A, int lda, const void* B, int ldb, void* o
   return run_norm_fused(A, lda, B, ldb, out, ldo, M, N, K, vec, ln_csum, ln_stats, ln_stats_tiles, ln_stats_width,
                         ln_eps, norm_groups, norm_width, norm_w0, norm_w1, norm_eps, rope_groups, rope_cos, rope_sin,
                         rope_ld, rows_per_batch, token_offset, static_cast<cudaStream_t>(stream), max_ctas);
+}
+
+int wdit_gemm_norm_exchange(const void* A, int lda, const void* B, int ldb, void* qk_scratch, int ld_scratch, int M,
+                            int K, const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                            int ln_stats_width, float ln_eps, const float* wq, const float* wk, float eps,
+                            const float* rope_cos, const float* rope_sin, int rope_ld, int batch, int Lp, int H,
+                            int P, int rank, const void* const* peer_bases, long long full_off, long long flag_off,
+                            unsigned int epoch, unsigned int* done_ctr, void* stream, int max_ctas) {
+  if (M == 0) return WDIT_OK;  // no rows: nothing to do (pointers are not looked at)
+  if (peer_bases == nullptr || done_ctr == nullptr || qk_scratch == nullptr) return WDIT_ERR_ARG;
+  if (H <= 0 || batch <= 0 || Lp <= 0 || P < 1 || P > kXchgMaxPeers || rank < 0 || rank >= P ||
+      (batch * H) % P != 0 || batch * Lp != M)
+    return WDIT_ERR_SHAPE;
+  const int D = H * 128;
+  const int N = 3 * D;
+  if (ld_scratch < N) return WDIT_ERR_SHAPE;
+  int rc = check_norm(A, lda, B, ldb, qk_scratch, ld_scratch, M, N, K, vec, 2, D, wq, wk, 2, rope_cos, rope_sin,
+                      rope_ld, Lp, rank * Lp);
+  if (rc) return rc;
+  if (D % BN != 0) return WDIT_ERR_SHAPE;
+  if ((full_off & 255) != 0 || (flag_off & 255) != 0) return WDIT_ERR_ALIGN;
+  XchgParams xc = {};
+  for (int q = 0; q < P; ++q) {
+    if (peer_bases[q] == nullptr || (reinterpret_cast<uintptr_t>(peer_bases[q]) & 255) != 0) return WDIT_ERR_ALIGN;
+    xc.base[q] = static_cast<unsigned char*>(const_cast<void*>(peer_bases[q]));
+  }
+  xc.full_off = full_off;
+  xc.flag_off = flag_off;
+  xc.done_ctr = done_ctr;
+  xc.epoch = epoch;
+  xc.P = P;
+  xc.rank = rank;
+  xc.B = batch;
+  xc.Lp = Lp;
+  xc.H = H;
+  xc.U = batch * H / P;
+  xc.L = P * Lp;
+  return run_norm_fused(A, lda, B, ldb, qk_scratch, ld_scratch, M, N, K, vec, ln_csum, ln_stats, ln_stats_tiles,
+                        ln_stats_width, ln_eps, 2, D, wq, wk, eps, 2, rope_cos, rope_sin, rope_ld, Lp, rank * Lp,
+                        static_cast<cudaStream_t>(stream), max_ctas, &xc);
 }
 
 }  // extern "C"

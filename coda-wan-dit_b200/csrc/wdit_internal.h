@@ -40,6 +40,21 @@ struct LnFold {
   float eps;
 };
 
+// Token-sharded runs: the norm GEMM sends its results straight into the ranks' exchange
+// regions (the Ulysses all-to-all of self-attention) instead of its own output buffer.
+// Unit u = b * H + h (batch entry b, head h) lives on rank u / U; rank r's region holds
+// full[3][U][L][128] bf16 (q, k, v of its units for all L = P * Lp tokens) at full_off and the
+// arrival flags u32[P] at flag_off. Disabled when P == 0.
+constexpr int kXchgMaxPeers = 8;
+struct XchgParams {
+  unsigned char* base[kXchgMaxPeers];  // every rank's exchange region, as mapped in this process
+  long long full_off;
+  long long flag_off;
+  unsigned int* done_ctr;  // this rank's CTA completion counter (zero between launches)
+  unsigned int epoch;      // published into flags[rank] of every region when all CTAs are done
+  int P, rank, B, Lp, H, U, L;
+};
+
 struct EpiParams {
   const float* vec;  // per-column bias / shift term [N], nullable
   LnFold ln;
@@ -60,6 +75,7 @@ struct EpiParams {
   int has_out_map;
   int has_x_map;
   NormParams norm;  // kEpiNorm only
+  XchgParams xchg;  // kEpiNorm only
 };
 
 // In-place full-width RMSNorm (+ RoPE) of the leading column groups of a bf16 matrix from

@@ -247,6 +247,38 @@ def gemm_norm(a, w, *, vec=None, ln: LnFold | None = None, norm_groups=0, norm_w
     return out
 
 
+def gemm_norm_exchange(a, w, *, vec, ln: LnFold | None, norm_w, norm_eps, rope_cos, rope_sin, batch, Lp, H, P,
+                       rank, peers, full_off, flag_off, epoch, done_ctr, scratch=None, max_ctas=0):
+    """Token-sharded QKV GEMM that delivers its output to the attention owners (wdit_gemm_norm_exchange).
+
+    a [batch*Lp, K] this rank's tokens; w [3*H*128, K]; q and k get the full-width RMSNorm
+    (weights norm_w) and the RoPE of their global tokens (rank*Lp + local token, tables with at
+    least P*Lp rows); q, k, v land in full[3][U][P*Lp][128] of the rank owning each
+    (batch, head) unit, in the exchange regions `peers` (ctypes array of P base addresses),
+    and `epoch` is published into flags[rank] of every region when the launch is done.
+    scratch [batch*Lp, 3*H*128] bf16 receives the pre-norm q / k (allocated when None).
+    """
+    _require_cuda(a, w)
+    a = _rowmajor(a)
+    M, K = a.shape
+    N = w.shape[0]
+    assert w.shape[1] == K and w.stride(1) == 1 and N == 3 * H * HEAD_DIM
+    if scratch is None:
+        scratch = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    assert rope_cos.shape == rope_sin.shape and rope_cos.shape[1] == HEAD_DIM // 2
+    assert rope_cos.dtype == torch.float32 and rope_sin.dtype == torch.float32
+    assert rope_cos.stride(1) == 1 and rope_sin.stride() == rope_cos.stride()
+    assert rope_cos.shape[0] >= P * Lp, "RoPE tables shorter than the sequence"
+    call(
+        "wdit_gemm_norm_exchange",
+        ptr(a), a.stride(0), ptr(w), w.stride(0), ptr(scratch), scratch.stride(0), M, K,
+        ptr(_f32vec(vec)), *_ln_args(ln, K), ptr(_f32vec(norm_w[0])), ptr(_f32vec(norm_w[1])), float(norm_eps),
+        ptr(rope_cos), ptr(rope_sin), rope_cos.stride(0), batch, Lp, H, P, rank, peers, full_off, flag_off,
+        epoch, done_ctr, stream_ptr(), max_ctas,
+    )
+    return scratch
+
+
 def ln_stats(x, *, stats_out=None, x_bf16_out=None, x_f32_out=None):
     """Per-256-column (mean, M2) of the rows of x [M, D] (bf16 or fp32)."""
     _require_cuda(x)

@@ -13,7 +13,11 @@ Two transports:
   exchanges are single kernels that store straight into peer memory over NVLink
   (wdit_p2p_qkv_exchange also applies the q/k RMSNorm + RoPE, so the QKV GEMM skips its own
   RMSNorm/RoPE pass), each followed by a bounded stream-ordered wait for all ranks' arrival
-  flags (wdit_p2p_wait).
+  flags (wdit_p2p_wait). With gemm_exchange=True the QKV GEMM itself is the first exchange
+  (wdit_gemm_norm_exchange: its epilogue normalizes q / k and stores q, k, v into the owners'
+  regions tile by tile). Off by default: on B200 it measures slower than the GEMM followed
+  by the exchange kernel (2 GPUs, cfg3: 241.7-243.4 vs 237.6 ms per forward), because the
+  epilogue's peer stores and normalize pass hold back the accumulator release.
 * "nccl": layout kernels (wdit_ulysses_pack / seq_gather / seq_scatter / ulysses_unpack) move
   the rows into contiguous per-peer blocks and torch.distributed.all_to_all_single (NCCL over
   NVLink / NVSwitch) moves the blocks.
@@ -26,7 +30,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
-from . import _lib
+from . import _lib, ops
 from ._lib import call, ptr, stream_ptr
 
 _HANDLE_BYTES = 64
@@ -107,7 +111,7 @@ class _Exchange:
 
 class SeqParallel:
     def __init__(self, group, world: int, rank: int, grid: tuple[int, int, int], seq_len: int,
-                 transport: str = "p2p"):
+                 transport: str = "p2p", gemm_exchange: bool = False):
         if seq_len % world != 0:
             raise ValueError(f"sequence length {seq_len} is not divisible by {world} ranks")
         if transport not in ("p2p", "nccl"):
@@ -120,6 +124,8 @@ class SeqParallel:
         self.local_len = seq_len // world
         self.token_offset = rank * self.local_len
         self.transport = transport
+        # QKV GEMM storing into the peers' regions itself (p2p transport only)
+        self.gemm_exchange = bool(gemm_exchange) and transport == "p2p"
         self._x: _Exchange | None = None
         self.epoch = 0
 
@@ -163,21 +169,50 @@ class SeqParallel:
         assert qkv.stride(1) == 1 and part.stride(1) == 1 and cos.stride(1) == 1 and sin.stride() == cos.stride()
         # the exchange reads the tables at global token positions up to P * Lp
         assert cos.shape[0] >= P * Lp and sin.shape[0] >= P * Lp, "RoPE tables shorter than the sequence"
-        if self._x is None or self._x.shape != (B, Lp, H, hd):
-            if self._x is not None:
-                self.close()
-            self._x = _Exchange(self, B, Lp, H, hd, qkv.device)
-        x = self._x
-        U, L, D = B * H // P, P * Lp, H * hd
+        x = self._region(B, Lp, H, hd, qkv.device)
         self.epoch += 1
         e, buf = self.epoch, self.epoch & 1
         st = stream_ptr()
         call("wdit_p2p_qkv_exchange", ptr(qkv), qkv.stride(0), ptr(part), part.stride(0), ptr(wq), ptr(wk),
              float(eps), ptr(cos), ptr(sin), cos.stride(0), B, Lp, H, hd, P, self.rank, x.peers,
              x.full_off[buf], x.flag_off[0], e, ptr(x.done), st)
+        return self._attend_and_return(x, buf, e, B, Lp, H, hd, key_lens, qkv.device)
+
+    def self_attention_gemm(self, a: torch.Tensor, w: torch.Tensor, vec: torch.Tensor, ln, wq: torch.Tensor,
+                            wk: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor, B: int, Lp: int,
+                            H: int, hd: int, key_lens=None) -> torch.Tensor:
+        """QKV projection + q/k RMSNorm / RoPE + the sequence-to-head exchange in one GEMM launch:
+        a [B*Lp, K] this rank's (bf16) tokens, w [3*H*hd, K] the folded QKV weight with its
+        per-column vec and LayerNorm fold ln -> attention output [B*Lp, H*hd] for the same
+        tokens. key_lens as for self_attention_p2p."""
+        P = self.world
+        assert self.gemm_exchange and Lp == self.local_len and (B * H) % P == 0 and hd == 128
+        assert cos.shape[0] >= P * Lp and sin.shape[0] >= P * Lp, "RoPE tables shorter than the sequence"
+        x = self._region(B, Lp, H, hd, a.device)
+        self.epoch += 1
+        e, buf = self.epoch, self.epoch & 1
+        ops.gemm_norm_exchange(a, w, vec=vec, ln=ln, norm_w=(wq, wk), norm_eps=eps, rope_cos=cos, rope_sin=sin,
+                               batch=B, Lp=Lp, H=H, P=P, rank=self.rank, peers=x.peers,
+                               full_off=x.full_off[buf], flag_off=x.flag_off[0], epoch=e, done_ctr=ptr(x.done))
+        return self._attend_and_return(x, buf, e, B, Lp, H, hd, key_lens, a.device)
+
+    def _region(self, B: int, Lp: int, H: int, hd: int, device) -> _Exchange:
+        if self._x is None or self._x.shape != (B, Lp, H, hd):
+            if self._x is not None:
+                self.close()
+            self._x = _Exchange(self, B, Lp, H, hd, device)
+        return self._x
+
+    def _attend_and_return(self, x: _Exchange, buf: int, e: int, B: int, Lp: int, H: int, hd: int, key_lens,
+                           device) -> torch.Tensor:
+        """Wait for every rank's q / k / v of epoch e, attend over this rank's units and send the
+        outputs back to the ranks owning their tokens."""
+        P = self.world
+        U, L, D = B * H // P, P * Lp, H * hd
+        st = stream_ptr()
         call("wdit_p2p_wait", x.flags(0), P, e, st)
         full = x.full(buf, U, L, hd)
-        mask = self.unit_key_mask(key_lens, B, H, L, qkv.device)
+        mask = self.unit_key_mask(key_lens, B, H, L, device)
         o = F.scaled_dot_product_attention(full[0].unsqueeze(0), full[1].unsqueeze(0), full[2].unsqueeze(0),
                                            attn_mask=mask)[0]
         assert o.stride(2) == 1

@@ -147,6 +147,33 @@ int wdit_gemm_norm_fused(const void* A, int lda, const void* B, int ldb, void* o
                          int max_ctas);
 
 /*
+ * Token-sharded (Ulysses) QKV with the all-to-all folded into the GEMM: the same math as
+ * wdit_gemm_norm_fused with N = 3 D, norm_groups = rope_groups = 2 (q, k) and rows_per_batch = Lp,
+ * but q, k (after RMSNorm / RoPE) and v are stored by the kernel straight into the exchange
+ * region of the rank that owns each (batch entry, head) unit, and the last CTA to finish
+ * writes `epoch` into flags[rank] of every rank's region (system-scope release). Replaces the
+ * QKV GEMM of coda_wan/run_wan_coda.py:158 plus the q/k norm kernel of
+ * coda_wan/wan_coda_kernels.py:355-368 and the sequence-to-head all-to-all that the
+ * reference's sequence-parallel attention does around them.
+ *   A [M = batch * Lp, K] is this rank's token shard (Lp tokens per batch entry, rank r holds
+ *     global tokens r * Lp .. r * Lp + Lp - 1); B [3 D, K] is the folded QKV weight; D = 128 H,
+ *     a multiple of 256; (batch * H) % P == 0, P <= 8.
+ *   qk_scratch [M, ld_scratch >= 3 D] bf16 on this GPU holds the pre-norm q, k.
+ *   peer_bases[P]: every rank's exchange region as mapped in this process (256-byte aligned).
+ *     Region layout from full_off: bf16 [3][U][L][128], U = batch * H / P units, L = P * Lp;
+ *     unit u = b * H + h lives on rank u / U. u32 flags[P] at flag_off.
+ *   done_ctr: one u32 on this GPU, zero before the first call; the kernel leaves it zero.
+ *   rope_cos / rope_sin: global-token tables with at least P * Lp rows.
+ * Returns WDIT_ERR_SHAPE / _ALIGN / _ARG for a bad argument (nothing launched).
+ */
+int wdit_gemm_norm_exchange(const void* A, int lda, const void* B, int ldb, void* qk_scratch, int ld_scratch, int M,
+                            int K, const float* vec, const float* ln_csum, const float* ln_stats, int ln_stats_tiles,
+                            int ln_stats_width, float ln_eps, const float* wq, const float* wk, float eps,
+                            const float* rope_cos, const float* rope_sin, int rope_ld, int batch, int Lp, int H,
+                            int P, int rank, const void* const* peer_bases, long long full_off, long long flag_off,
+                            unsigned int epoch, unsigned int* done_ctr, void* stream, int max_ctas);
+
+/*
  * wdit_gemm_norm without a workspace argument: it allocates nothing and takes no scratch from
  * the caller. No counterpart in the reference (which always allocates through PyTorch); it is
  * for callers that cannot allocate device memory where they issue this GEMM, e.g. code running

@@ -88,6 +88,33 @@ def test_p2p_argument_validation_without_device(lib):
     assert lib.wdit_ipc_open(null, None) == 1
 
 
+def test_gemm_norm_exchange_validates_without_device(lib):
+    null = ctypes.c_void_p(None)
+    d = ctypes.c_void_p(0x1000)
+    peers = (ctypes.c_void_p * 2)(0x100000, 0x200000)
+
+    def call(*, A=d, scratch=d, ld=4608, M=192, batch=2, Lp=96, H=12, P=2, rank=0, bases=peers, full_off=0,
+             flag_off=0, ctr=d):
+        return lib.wdit_gemm_norm_exchange(A, 1536, d, 1536, scratch, ld, M, 1536, d, null, null, 0, 0, 0.0, d, d,
+                                           1e-6, d, d, 64, batch, Lp, H, P, rank, bases, full_off, flag_off, 1, ctr,
+                                           null, 0)
+
+    assert call(M=0) == 0                           # no rows: nothing to do
+    assert call(A=null) == 1                        # null operand
+    assert call(scratch=null) == 1
+    assert call(ctr=null) == 1
+    assert call(bases=None) == 1
+    assert call(M=190) == 2                         # batch * Lp != M
+    assert call(H=5, ld=1920, P=4) == 2             # 10 (batch, head) units do not divide over 4 ranks
+    assert call(rank=2) == 2                        # rank outside [0, P)
+    assert call(P=9) == 2                           # more ranks than the kernel's peer table
+    assert call(ld=3072) == 2                       # scratch narrower than 3 D
+    assert call(full_off=100) == 3                  # region offsets not 256-byte aligned
+    assert call(flag_off=4) == 3
+    bad = (ctypes.c_void_p * 2)(0x100000, 0x200010)
+    assert call(bases=bad) == 3                     # a peer region not 256-byte aligned
+
+
 def test_batched_entry_points_validate_without_device(lib, pkg):
     null = ctypes.c_void_p(None)
     dummy = ctypes.c_void_p(0x1000)

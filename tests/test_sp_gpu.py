@@ -1,6 +1,7 @@
-"""Token-sharded (sequence-parallel) forward on 2 GPUs, NCCL Ulysses all-to-all: every rank's
-output shard equals the same tokens of the single-GPU forward (same weights and inputs).
-Skipped when fewer than 2 GPUs are visible."""
+"""Token-sharded (sequence-parallel) forward on 2 GPUs: every rank's output shard equals the same
+tokens of the single-GPU forward (same weights and inputs), for each Ulysses transport: NVLink
+peer stores with the QKV GEMM storing into the peers itself (gemm_exchange), peer stores by
+the separate exchange kernel, and the NCCL all-to-all. Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -32,7 +33,7 @@ def _inputs(cfg, dev, padded=False):
     return inp
 
 
-def _worker(rank, world, port, root, transport, padded, ret):
+def _worker(rank, world, port, root, transport, padded, gemm_exchange, ret):
     import sys
     from datetime import timedelta
 
@@ -52,7 +53,7 @@ def _worker(rank, world, port, root, transport, padded, ret):
         inp = _inputs(cfg, dev, padded)
         L = inp["seq_len"]
         sp = pkg.SeqParallel(dist.group.WORLD, world, rank, (LATENT[0], LATENT[1] // 2, LATENT[2] // 2), L,
-                             transport=transport)
+                             transport=transport, gemm_exchange=gemm_exchange)
         params = pkg.build_wan(pkg.WAN_1_3B, seed=11, device=dev, num_layers=LAYERS)
         model = pkg.FusedWanModel(params, sp)
         with torch.no_grad():
@@ -67,8 +68,11 @@ def _worker(rank, world, port, root, transport, padded, ret):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport,padded", [("p2p", False), ("nccl", False), ("p2p", True), ("nccl", True)])
-def test_sequence_parallel_matches_single_gpu(pkg, transport, padded):
+@pytest.mark.parametrize("transport,padded,gemm_exchange", [
+    ("p2p", False, True), ("p2p", False, False), ("nccl", False, False),
+    ("p2p", True, True), ("p2p", True, False), ("nccl", True, False),
+])
+def test_sequence_parallel_matches_single_gpu(pkg, transport, padded, gemm_exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from pathlib import Path
@@ -84,8 +88,8 @@ def test_sequence_parallel_matches_single_gpu(pkg, transport, padded):
     with torch.no_grad():
         full = pkg.FusedWanModel(params)(inp["x"], inp["t"], inp["context"], L, return_tokens=True).float().cpu()
     ret = mp.Manager().dict()
-    mp.start_processes(_worker, args=(2, _port(), root, transport, padded, ret), nprocs=2, start_method="spawn",
-                       join=True)
+    mp.start_processes(_worker, args=(2, _port(), root, transport, padded, gemm_exchange, ret), nprocs=2,
+                       start_method="spawn", join=True)
     Lp = L // 2
     for r in range(2):
         want = full[:, r * Lp:(r + 1) * Lp]

@@ -26,6 +26,7 @@ Activations (> 1 GB per step) exceed the 126 MB L2, so no explicit flush is need
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -238,6 +239,22 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+@contextlib.contextmanager
+def stdout_to_stderr():
+    """Send everything written to file descriptor 1 meanwhile to stderr. torch.compile's
+    max-autotune prints its tuning tables, JSON-formatted lines among them, to stdout; the
+    benchmark's stdout must carry only its own result line."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    try:
+        os.dup2(2, 1)
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def oracle_gpu_baselines(pkg, w: dict, state: dict, layers: int, args_fwd, iters: int, warmup: int,
                          compile_mode: str | None) -> dict:
     """The reference's two GPU baselines on this GPU with this run's weights and inputs: the
@@ -266,7 +283,7 @@ def oracle_gpu_baselines(pkg, w: dict, state: dict, layers: int, args_fwd, iters
 
     res = {"what": "stock-Wan forward restated in eager PyTorch (oracle), bf16 mixed precision, same weights "
                    "and inputs, same GPU", "iters": iters, "warmup": warmup}
-    with torch.no_grad():
+    with torch.no_grad(), stdout_to_stderr():
         res["eager_ms"] = median_ms(lambda: stock(*args_fwd))
         if compile_mode:
             # a compiler failure must not cost the benchmark line: it is reported instead

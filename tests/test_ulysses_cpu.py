@@ -152,3 +152,44 @@ def test_unit_key_mask_none_without_padding(pkg):
     m = pkg.SeqParallel(None, 8, 5, (1, 1, 64), 64, transport="nccl").unit_key_mask([64, 40], 2, 12, 64, "cpu")
     # rank 5 holds units 15, 16, 17 (batch 1): keys 40.. masked
     assert bool(m[..., :40].all()) and not bool(m[..., 40:].any())
+
+
+def _direct_store_offsets(rank, B, Lp, H, P, mat):
+    """The peer-store address rule of the exchanging kernels (xchg_addr in csrc/gemm.cu and the
+    same rule in csrc/p2p.cu), restated: element (row, column c) of matrix `mat` of rank
+    `rank`'s QKV output goes to rank pr's region, element offset ((mat*U + ul)*L + gtok)*128 +
+    c % 128, with unit u = b*H + c // 128, pr = u // U, ul = u % U, gtok = rank*Lp + token."""
+    U, L, D = B * H // P, P * Lp, H * 128
+    row = torch.arange(B * Lp).view(-1, 1)
+    c = torch.arange(D).view(1, -1)
+    b = row // Lp
+    u = b * H + (c >> 7)
+    pr = u // U
+    ul = u - pr * U
+    gtok = rank * Lp + (row - b * Lp)
+    return pr, ((mat * U + ul) * L + gtok) * 128 + (c & 127)
+
+
+@pytest.mark.parametrize("B,H,P,Lp", [(2, 12, 2, 5), (2, 12, 4, 3), (2, 12, 8, 2), (1, 12, 4, 3), (2, 40, 8, 2)])
+def test_direct_peer_stores_land_where_the_gather_puts_them(B, H, P, Lp):
+    """Stores made with the address rule cover every slot of every rank's q/k/v region exactly
+    once and leave there what pack -> all_to_all -> seq_gather (the layout oracle) produces."""
+    torch.manual_seed(1)
+    U, L, D = B * H // P, P * Lp, H * 128
+    rows = [torch.randn(B * Lp, 3 * D) for _ in range(P)]
+    region = [torch.full((3 * U * L * 128,), float("nan")) for _ in range(P)]
+    hits = [torch.zeros(3 * U * L * 128, dtype=torch.int64) for _ in range(P)]
+    for r in range(P):
+        for mat in range(3):
+            pr, off = _direct_store_offsets(r, B, Lp, H, P, mat)
+            vals = rows[r][:, mat * D:(mat + 1) * D]
+            for d in range(P):
+                sel = pr == d
+                region[d][off[sel]] = vals[sel]
+                hits[d].index_add_(0, off[sel], torch.ones_like(off[sel]))
+    sends = [ulysses_ref.pack(rows[r], B, Lp, H, 128, 3, P) for r in range(P)]
+    for d in range(P):
+        assert torch.equal(hits[d], torch.ones_like(hits[d])), d
+        recv = torch.stack([sends[p][d] for p in range(P)])  # what all_to_all delivers to rank d
+        want = ulysses_ref.seq_gather(recv, 3, U, P, Lp, 128)
+        assert torch.equal(region[d].view(3, U, L, 128), want), d

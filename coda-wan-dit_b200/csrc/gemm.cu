@@ -569,6 +569,7 @@ __global__ void __launch_bounds__(num_threads<KIND>(), 1)
 
     if constexpr (KIND == kEpiAct || KIND == kEpiNorm) {
       constexpr int kChunks = (BN / 2) / 32;  // 32-column chunks per half
+      static_assert(kChunks % 2 == 0, "exchange stores pair up the chunks of a half");
       // Per-warp staging: two 32-row x 32-column bf16 buffers (64-byte swizzle) per warp, each
       // stored by the warp's own TMA store, so the warps of a half never wait on each other.
       uint8_t* stg_warp_ptr = epi_base + ew * 2 * kWarpStgBytes;
@@ -670,15 +671,37 @@ __global__ void __launch_bounds__(num_threads<KIND>(), 1)
             }
           }
           if (KIND == kEpiNorm && upos < 0 && p.xchg.P > 0) {
-            // Token-sharded run: a plain (v) tile goes straight from registers into the exchange
-            // region of the rank owning its unit, 64 contiguous bytes per row.
-            if (row_ok) {
-              const XchgParams& xc = p.xchg;
-              const int b = row / xc.Lp;
-              const int gtok = xc.rank * xc.Lp + (row - b * xc.Lp);
-              unsigned char* dst = xchg_addr(xc, 2, b, gtok, n0 - s.norm_groups * p.norm.width);
+            // Token-sharded run: a plain (v) tile goes into the exchange region of the rank
+            // owning its unit. Two consecutive chunks fill the warp's two staging buffers as one
+            // 32-row x 128-byte block (16-byte pieces XOR-swizzled by row); the block then
+            // leaves as whole 128-byte lines, 4 rows per store instruction (a head's token row
+            // is 256 contiguous bytes at the destination, so each line is one NVLink write).
+            const int pbase = (c & 1) * 4;
+            if (pbase == 0) {
+              if (lane == 0) bulk_wait_read<0>();  // earlier TMA stores have read the buffers
+              __syncwarp();
+            }
 #pragma unroll
-              for (int q = 0; q < 4; ++q) st_global_v4(dst + 16 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+            for (int q = 0; q < 4; ++q)
+              st_shared_v4(stg_warp + lane * 128 + (((pbase + q) ^ (lane & 7)) << 4), w[4 * q], w[4 * q + 1],
+                           w[4 * q + 2], w[4 * q + 3]);
+            if (pbase != 0) {
+              __syncwarp();
+              const XchgParams& xc = p.xchg;
+              const int vcol = n0 - 32 - s.norm_groups * p.norm.width;  // first column of the pair
+              const int pc = lane & 7;
+#pragma unroll 2
+              for (int i = 0; i < 8; ++i) {
+                const int rr = 4 * i + (lane >> 3);
+                const uint4 val = ld_shared_u4(stg_warp + rr * 128 + ((pc ^ (rr & 7)) << 4));
+                const int grow = warp_row0 + rr;
+                if (grow < s.M) {
+                  const int b = grow / xc.Lp;
+                  const int gtok = xc.rank * xc.Lp + (grow - b * xc.Lp);
+                  st_global_v4(xchg_addr(xc, 2, b, gtok, vcol) + pc * 16, val.x, val.y, val.z, val.w);
+                }
+              }
+              __syncwarp();  // the block is read out before the next chunk is staged
             }
             continue;
           }

@@ -436,6 +436,15 @@ __device__ __forceinline__ void ld_shared_v4(uint32_t addr, float& a, float& b, 
                : "memory");
 }
 
+__device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 // 16-byte global load cached in L2 only (data another thread of the CTA just wrote).
 __device__ __forceinline__ uint4 ld_global_cg_v4(const void* p) {
   uint4 r;

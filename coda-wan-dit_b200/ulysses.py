@@ -15,9 +15,10 @@ Two transports:
   RMSNorm/RoPE pass), each followed by a bounded stream-ordered wait for all ranks' arrival
   flags (wdit_p2p_wait). With gemm_exchange=True the QKV GEMM itself is the first exchange
   (wdit_gemm_norm_exchange: its epilogue normalizes q / k and stores q, k, v into the owners'
-  regions tile by tile). Off by default: on B200 it measures slower than the GEMM followed
-  by the exchange kernel (2 GPUs, cfg3: 241.7-243.4 vs 237.6 ms per forward), because the
-  epilogue's peer stores and normalize pass hold back the accumulator release.
+  regions tile by tile). Off by default: on B200 it measures slightly slower than the GEMM
+  followed by the exchange kernel (2 GPUs, cfg3: 237.4-237.9 vs 235.9-236.4 ms per forward),
+  because the epilogue's peer stores hold back the accumulator release instead of
+  overlapping with the tensor-core work.
 * "nccl": layout kernels (wdit_ulysses_pack / seq_gather / seq_scatter / ulysses_unpack) move
   the rows into contiguous per-peer blocks and torch.distributed.all_to_all_single (NCCL over
   NVLink / NVSwitch) moves the blocks.

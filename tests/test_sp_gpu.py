@@ -1,7 +1,8 @@
-"""Token-sharded (sequence-parallel) forward on 2 GPUs: every rank's output shard equals the same
-tokens of the single-GPU forward (same weights and inputs), for each Ulysses transport: NVLink
-peer stores with the QKV GEMM storing into the peers itself (gemm_exchange), peer stores by
-the separate exchange kernel, and the NCCL all-to-all. Skipped when fewer than 2 GPUs are visible."""
+"""Token-sharded (sequence-parallel) forward on 2 (and 4) GPUs: every rank's output shard equals
+the same tokens of the single-GPU forward (same weights and inputs), for each Ulysses transport:
+NVLink peer stores with the QKV GEMM storing into the peers itself (gemm_exchange), peer stores
+by the separate exchange kernel, and the NCCL all-to-all. Cases needing more GPUs than are
+visible are skipped."""
 import os
 import socket
 
@@ -68,13 +69,14 @@ def _worker(rank, world, port, root, transport, padded, gemm_exchange, ret):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport,padded,gemm_exchange", [
-    ("p2p", False, True), ("p2p", False, False), ("nccl", False, False),
-    ("p2p", True, True), ("p2p", True, False), ("nccl", True, False),
+@pytest.mark.parametrize("world,transport,padded,gemm_exchange", [
+    (2, "p2p", False, True), (2, "p2p", False, False), (2, "nccl", False, False),
+    (2, "p2p", True, True), (2, "p2p", True, False), (2, "nccl", True, False),
+    (4, "p2p", False, True), (4, "p2p", False, False), (4, "p2p", True, True),
 ])
-def test_sequence_parallel_matches_single_gpu(pkg, transport, padded, gemm_exchange):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def test_sequence_parallel_matches_single_gpu(pkg, world, transport, padded, gemm_exchange):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from pathlib import Path
 
     from oracle import wan_ref
@@ -88,10 +90,10 @@ def test_sequence_parallel_matches_single_gpu(pkg, transport, padded, gemm_excha
     with torch.no_grad():
         full = pkg.FusedWanModel(params)(inp["x"], inp["t"], inp["context"], L, return_tokens=True).float().cpu()
     ret = mp.Manager().dict()
-    mp.start_processes(_worker, args=(2, _port(), root, transport, padded, gemm_exchange, ret), nprocs=2,
+    mp.start_processes(_worker, args=(world, _port(), root, transport, padded, gemm_exchange, ret), nprocs=world,
                        start_method="spawn", join=True)
-    Lp = L // 2
-    for r in range(2):
+    Lp = L // world
+    for r in range(world):
         want = full[:, r * Lp:(r + 1) * Lp]
         got, got2 = ret[r]
         rel = ((got - want).norm() / want.norm()).item()

@@ -328,7 +328,7 @@ def run_ours(args) -> None:
     params = pkg.build_wan(getattr(pkg, w["shape"]), seed=SEED, device=dev, num_layers=layers)
     # The weights as built (before the fused blocks re-point the parameters at packed storage),
     # for the stock-Wan comparison forwards after the timed regions.
-    want_oracle = world == 1 and not args.no_oracle and args.workload == "cfg3"
+    want_oracle = world == 1 and not args.no_oracle and (args.workload == "cfg3" or args.oracle)
     state = dict(params.state_dict()) if want_oracle else None
     model = pkg.FusedWanModel(params, sp)
 
@@ -501,13 +501,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-oracle", action="store_true",
                     help="skip the stock-Wan eager / torch.compile forwards on the GPU (N = 1, cfg3)")
+    ap.add_argument("--oracle", action="store_true",
+                    help="also run the stock-Wan eager / torch.compile forwards for workloads other than cfg3")
     ap.add_argument("--no-compile", action="store_true", help="skip only the torch.compile forward")
     ap.add_argument("--oracle-iters", type=int, default=5)
     ap.add_argument("--transport", choices=("p2p", "nccl"), default="p2p",
                     help="Ulysses all-to-all: NVLink peer stores (p2p) or NCCL all_to_all_single")
     ap.add_argument("--gemm-exchange", action="store_true",
                     help="p2p: the QKV GEMM stores q / k / v into the peers itself instead of a separate "
-                         "exchange kernel after it (0.5% slower on B200 at 2 GPUs, kept as an option)")
+                         "exchange kernel after it (0.5%% slower on B200 at 2 GPUs, kept as an option)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

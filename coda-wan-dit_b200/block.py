@@ -345,51 +345,46 @@ class FusedWanBlock(nn.Module):
         # either the QKV GEMM stores into the owners' regions itself (one segment), or the GEMM
         # only emits the raw projection and its mean-square partials for the exchange kernel.
         fused_exchange = sp is not None and sp.fuses_qk_norm
-        gemm_exchange = fused_exchange and sp.gemm_exchange and nseg == 1 and D % 256 == 0
-        if gemm_exchange:
-            nseg = 0
-            if folds is not None:
-                wf, cs, vec = folds[0]
-            else:
-                wf, cs, vec = ops.fold_weight(self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=e_row(0, 1),
-                                              shift_a=mod[0], shift_b=e_row(0, 0), bias=self.b_qkv)
+        if fused_exchange and sp.gemm_exchange and nseg == 1 and D % 256 == 0:
+            wf, cs, vec = folds[0] if folds is not None else ops.fold_weight(
+                self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=e_row(0, 1), shift_a=mod[0], shift_b=e_row(0, 0),
+                bias=self.b_qkv)
             y = sp.self_attention_gemm(xb, wf, vec, ops.LnFold(cs, stats, self.eps), self.w_nq, self.w_nk,
                                        self.rms_eps, cos, sin, B, L, H, hd, key_lens=_host_values(seq_lens))
         else:
             qkv = torch.empty((M, 3 * D), dtype=torch.bfloat16, device=dev)
-        part = torch.empty((M, 2 * D // ops.RMS_BLOCK), dtype=torch.float32, device=dev) \
-            if fused_exchange and not gemm_exchange else None
-        for sg in range(nseg):
-            r0, r1 = (0, M) if nseg == 1 else (sg * L, (sg + 1) * L)
-            b = sg if Be > 1 else 0  # modulation row of this segment
-            if folds is not None:
-                wf, cs, vec = folds[2 * b]
-            else:
-                wf, cs, vec = ops.fold_weight(self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=e_row(b, 1),
-                                              shift_a=mod[0], shift_b=e_row(b, 0), bias=self.b_qkv)
-            ln = ops.LnFold(cs, stats[r0:r1], self.eps)
+            part = torch.empty((M, 2 * D // ops.RMS_BLOCK), dtype=torch.float32, device=dev) \
+                if fused_exchange else None
+            for sg in range(nseg):
+                r0, r1 = (0, M) if nseg == 1 else (sg * L, (sg + 1) * L)
+                b = sg if Be > 1 else 0  # modulation row of this segment
+                if folds is not None:
+                    wf, cs, vec = folds[2 * b]
+                else:
+                    wf, cs, vec = ops.fold_weight(self.w_qkv, mult_c=1.0, mult_a=mod[1], mult_b=e_row(b, 1),
+                                                  shift_a=mod[0], shift_b=e_row(b, 0), bias=self.b_qkv)
+                ln = ops.LnFold(cs, stats[r0:r1], self.eps)
+                if fused_exchange:
+                    ops.gemm_act(xb[r0:r1], wf, vec=vec, ln=ln, out=qkv[r0:r1], ms_out=part[r0:r1], ms_cols=2 * D)
+                    continue
+                seg_cos, seg_sin = (cos, sin) if sample_grids is None else \
+                    self._rope_tables(sample_grids[sg], freqs, L)
+                ops.gemm_norm(
+                    xb[r0:r1], wf, vec=vec, ln=ln, norm_groups=2, norm_width=D,
+                    norm_w=(self.w_nq, self.w_nk), norm_eps=self.rms_eps, rope_groups=2, rope_cos=seg_cos,
+                    rope_sin=seg_sin, rows_per_batch=grid_rows_per_batch, token_offset=token_offset,
+                    out=qkv[r0:r1], workspace=self.workspace,
+                )
             if fused_exchange:
-                ops.gemm_act(xb[r0:r1], wf, vec=vec, ln=ln, out=qkv[r0:r1], ms_out=part[r0:r1], ms_cols=2 * D)
-                continue
-            seg_cos, seg_sin = (cos, sin) if sample_grids is None else self._rope_tables(sample_grids[sg], freqs, L)
-            ops.gemm_norm(
-                xb[r0:r1], wf, vec=vec, ln=ln, norm_groups=2, norm_width=D,
-                norm_w=(self.w_nq, self.w_nk), norm_eps=self.rms_eps, rope_groups=2, rope_cos=seg_cos,
-                rope_sin=seg_sin, rows_per_batch=grid_rows_per_batch, token_offset=token_offset, out=qkv[r0:r1],
-                workspace=self.workspace,
-            )
-        if gemm_exchange:
-            pass  # y came from the exchanging GEMM
-        elif fused_exchange:
-            y = sp.self_attention_p2p(qkv, part, self.w_nq, self.w_nk, self.rms_eps, cos, sin, B, L, H, hd,
-                                      key_lens=_host_values(seq_lens))
-        elif sp is not None:
-            y = sp.self_attention(qkv, B, L, H, hd, key_lens=_host_values(seq_lens))
-        else:
-            q = qkv[:, :D].view(B, L, H, hd)
-            k = qkv[:, D:2 * D].view(B, L, H, hd)
-            v = qkv[:, 2 * D:].view(B, L, H, hd)
-            y = local_attention(q, k, v, seq_lens).reshape(M, D)
+                y = sp.self_attention_p2p(qkv, part, self.w_nq, self.w_nk, self.rms_eps, cos, sin, B, L, H, hd,
+                                          key_lens=_host_values(seq_lens))
+            elif sp is not None:
+                y = sp.self_attention(qkv, B, L, H, hd, key_lens=_host_values(seq_lens))
+            else:
+                q = qkv[:, :D].view(B, L, H, hd)
+                k = qkv[:, D:2 * D].view(B, L, H, hd)
+                v = qkv[:, 2 * D:].view(B, L, H, hd)
+                y = local_attention(q, k, v, seq_lens).reshape(M, D)
         ops.gemm_residual(
             y, self.w_o, x32, out=x32, bias=self.b_o, gate_a=mod[2], gate_b=ev[:, 2 * D:], gate_b_stride=gate_stride,
             rows_per_batch=rows_per_batch, x_bf16_out=xb, stats_out=stats,

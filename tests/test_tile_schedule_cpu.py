@@ -100,3 +100,34 @@ def test_grouped_rasterization_bounds_the_tiles_in_flight():
     for start in range(0, mg * nb - 74, 997):
         window = [raster(t, mg, nb) for t in range(start, start + 74)]
         assert len({m for m, _ in window}) <= 16 and len({n for _, n in window}) <= 11
+
+
+def test_exchange_v_staging_layout():
+    """The exchange GEMM's v staging (gemm.cu, kEpiNorm with peer stores): lane l (row l of the
+    warp's 32) writes its 16-byte piece p (0-7: two 32-column chunks) at l*128 + ((p ^ (l & 7))
+    << 4) of the warp's 4 KB; store step i has lane l read row 4i + l/8, piece l % 8. Every read
+    gets the piece its (row, piece) names, each step covers 4 whole 128-byte rows (one line per
+    8 lanes), and every quarter-warp's 8 accesses hit 8 distinct 16-byte bank groups (no shared
+    memory bank conflict)."""
+    def addr(row, piece):
+        return row * 128 + ((piece ^ (row & 7)) << 4)
+
+    written = {}
+    for piece in range(8):
+        addrs = [addr(lane, piece) for lane in range(32)]
+        for q in range(4):  # quarter-warps
+            assert len({(a % 128) // 16 for a in addrs[8 * q:8 * q + 8]}) == 8
+        for lane, a in enumerate(addrs):
+            assert a not in written
+            written[a] = (lane, piece)
+    assert sorted(written) == list(range(0, 4096, 16))
+    for i in range(8):
+        got = []
+        for lane in range(32):
+            row, piece = 4 * i + (lane >> 3), lane & 7
+            a = addr(row, piece)
+            assert written[a] == (row, piece)
+            got.append((row, piece))
+        for q in range(4):
+            assert len({(addr(*rp) % 128) // 16 for rp in got[8 * q:8 * q + 8]}) == 8
+            assert {rp[0] for rp in got[8 * q:8 * q + 8]} == {4 * i + q}  # one whole row per 8 lanes
